@@ -1,0 +1,271 @@
+/*
+ * ds3_cuda.h — B200 (sm_100a) backend C-ABI for the qw3 engine's fused
+ * per-layer path.
+ *
+ * The engine (src/ds3_engine.c of wzqhbustb/qw3) calls its GPU backend through
+ * src/ds3_metal.h. This header offers the same entry points under a ds3_cuda_
+ * prefix, with the same argument order, meaning and return convention, so the
+ * engine can swap backends per op; each declaration cites the ds3_metal.h
+ * line it replaces. Entries marked "new" have no Metal counterpart: they are
+ * the fused kernels of this backend (one pass over HBM where the Metal path
+ * makes two or three) and the stream/graph/timer plumbing a CUDA host needs.
+ *
+ * Conventions (as ds3_metal.m):
+ *  - ops return 0 on success, -1 on error; allocators return NULL on failure;
+ *    errors are printed to stderr;
+ *  - rows are dense (row stride = n * element size);
+ *  - in-place calls are legal where the Metal engine makes them
+ *    (rms_norm(x, w, x), rope(src == dst), qk_norm_rope in place);
+ *  - outside begin_batch/end_batch every op is synchronous: it launches,
+ *    waits for the device and returns the status; inside a batch (or a graph
+ *    capture) ops only enqueue, and end_batch waits and returns the status;
+ *  - one device context per process (multi-GPU = one process per GPU; call
+ *    ds3_cuda_set_device before ds3_cuda_init); state is not thread-safe.
+ *
+ * Device-side errors (a token id outside the vocabulary, a bounded wait that
+ * ran out) never trap: the kernel skips the bad row, writes zeros there and
+ * sets a bit in a device error word, which the next synchronising call reads,
+ * reports and clears (it then returns -1).
+ */
+#ifndef DS3_CUDA_H
+#define DS3_CUDA_H
+
+#include <stdint.h>
+#include <stddef.h>
+#include <stdbool.h>
+
+#if defined(__has_include)
+#  if __has_include("ds3.h")
+#    include "ds3.h"
+#  endif
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifndef DS3_H
+/* GGUF tensor type ids; same values as ds3_type_t in the engine's src/ds3.h:201-216.
+ * (When the engine's ds3.h is on the include path its enum is used instead.) */
+typedef enum {
+    DS3_TYPE_F32  = 0,
+    DS3_TYPE_F16  = 1,
+    DS3_TYPE_Q8_0 = 8,
+    DS3_TYPE_Q4_K = 12,
+    DS3_TYPE_Q6_K = 14
+} ds3_type_t;
+#endif
+
+/* Opaque handle to a device buffer (ds3_metal.h:14). A view shares its
+ * parent's allocation; freeing a view never frees the parent. */
+typedef struct ds3_cuda_buffer ds3_cuda_buffer_t;
+
+/* ------------------------------------------------------------------ */
+/* Lifecycle                                                          */
+/* ------------------------------------------------------------------ */
+
+/* new: select the CUDA device this process drives; call before init. */
+int  ds3_cuda_set_device(int device);
+/* ds3_metal.h:19-20. Returns 0, or -1 if no usable sm_100 device is present. */
+int  ds3_cuda_init(void);
+void ds3_cuda_shutdown(void);
+
+/* ------------------------------------------------------------------ */
+/* Buffers                                                            */
+/* ------------------------------------------------------------------ */
+
+/* ds3_metal.h:25-26 */
+ds3_cuda_buffer_t *ds3_cuda_buffer_alloc(size_t bytes);
+void               ds3_cuda_buffer_free(ds3_cuda_buffer_t *buf);
+/* ds3_metal.h:31. Metal aliases the mmap on unified memory; here the region is
+ * copied once into device memory (a host-resident table would bound every
+ * gather by the host link, not HBM). The result is read-only. `base` need not
+ * be page-aligned. */
+ds3_cuda_buffer_t *ds3_cuda_buffer_from_mmap(const void *base, size_t bytes);
+/* ds3_metal.h:35-36 */
+ds3_cuda_buffer_t *ds3_cuda_buffer_view(const ds3_cuda_buffer_t *base,
+                                        size_t offset, size_t bytes);
+/* new: wrap device memory owned by someone else (e.g. a framework tensor);
+ * free() releases only the handle. */
+ds3_cuda_buffer_t *ds3_cuda_buffer_wrap(void *device_ptr, size_t bytes);
+/* new: device address and size of a buffer (views included). */
+void  *ds3_cuda_buffer_device_ptr(const ds3_cuda_buffer_t *buf);
+size_t ds3_cuda_buffer_size(const ds3_cuda_buffer_t *buf);
+/* ds3_metal.h:39-42. Synchronous copies on the module stream. Writes to
+ * read-only (from_mmap) buffers are refused. Inside a batch they are ordered
+ * after the ops already enqueued. */
+int ds3_cuda_buffer_write(ds3_cuda_buffer_t *buf, size_t offset,
+                          const void *src, size_t bytes);
+int ds3_cuda_buffer_read (ds3_cuda_buffer_t *buf, size_t offset,
+                          void *dst, size_t bytes);
+
+/* ------------------------------------------------------------------ */
+/* Ops with a ds3_metal.h counterpart                                 */
+/* ------------------------------------------------------------------ */
+
+/* ds3_metal.h:53-57. out = x / sqrt(mean(x^2) + eps) * weight, per row. */
+int ds3_cuda_rms_norm(const ds3_cuda_buffer_t *x,
+                      const ds3_cuda_buffer_t *weight,
+                      ds3_cuda_buffer_t       *out,
+                      uint32_t n, uint32_t n_rows, float eps);
+
+/* ds3_metal.h:64-69. NEOX RoPE over [n_rows, n_heads*head_dim]; positions int32 [n_rows]. */
+int ds3_cuda_rope(const ds3_cuda_buffer_t *src,
+                  ds3_cuda_buffer_t       *dst,
+                  const ds3_cuda_buffer_t *positions,
+                  uint32_t n_heads, uint32_t head_dim, uint32_t n_rows,
+                  float theta_base);
+
+/* ds3_metal.h:168-178 */
+int ds3_cuda_buffer_copy_f32(const ds3_cuda_buffer_t *src, ds3_cuda_buffer_t *dst, size_t bytes);
+int ds3_cuda_buffer_zero_f32(ds3_cuda_buffer_t *buf, size_t bytes);
+int ds3_cuda_vec_add_inplace(ds3_cuda_buffer_t *acc, const ds3_cuda_buffer_t *addend, uint32_t n);
+int ds3_cuda_vec_add(const ds3_cuda_buffer_t *a, const ds3_cuda_buffer_t *b,
+                     ds3_cuda_buffer_t *c, uint32_t n);
+
+/* ds3_metal.h:184-192. gather: dst[i] = src[ids[offset+i]];
+ * scatter: dst[ids[offset+i]] += scores[offset+i] * src[i] (ids unique per call). */
+int ds3_cuda_gather_rows_f32(const ds3_cuda_buffer_t *src, const ds3_cuda_buffer_t *ids,
+                             ds3_cuda_buffer_t *dst,
+                             uint32_t n_cols, uint32_t count, uint32_t offset);
+int ds3_cuda_scatter_add_weighted_f32(const ds3_cuda_buffer_t *src,
+                                      const ds3_cuda_buffer_t *scores,
+                                      const ds3_cuda_buffer_t *ids,
+                                      ds3_cuda_buffer_t *dst,
+                                      uint32_t n_cols, uint32_t count, uint32_t offset);
+
+/* ds3_metal.h:195-198. out = silu(gate) * up. */
+int ds3_cuda_silu_mul_f32(const ds3_cuda_buffer_t *gate, const ds3_cuda_buffer_t *up,
+                          ds3_cuda_buffer_t *out, uint32_t n);
+
+/* ds3_metal.h:424-431. logits [n_layers][n_expert] -> indices/scores [n_layers][n_used]. */
+int ds3_cuda_moe_router_topk_batch(const ds3_cuda_buffer_t *logits,
+                                   ds3_cuda_buffer_t *indices, ds3_cuda_buffer_t *scores,
+                                   uint32_t n_layers, uint32_t n_expert, uint32_t n_used,
+                                   bool norm_topk_prob);
+/* ds3_metal.h:437-445. logits [n_layers][n_tokens][n_expert] ->
+ * [n_layers][n_tokens][n_used] (dense layer stride n_tokens*n_used). */
+int ds3_cuda_moe_router_topk_batch_tokens(const ds3_cuda_buffer_t *logits,
+                                          ds3_cuda_buffer_t *indices, ds3_cuda_buffer_t *scores,
+                                          uint32_t n_layers, uint32_t n_tokens,
+                                          uint32_t n_expert, uint32_t n_used,
+                                          bool norm_topk_prob);
+
+/* ds3_metal.h:457-462. begin_batch returns -1 if a batch is already open. */
+int  ds3_cuda_begin_batch(void);
+int  ds3_cuda_end_batch(void);
+void ds3_cuda_synchronize(void);
+
+/* ds3_metal.h:467-468. Enabled with DS3_CUDA_PROFILE=1 (or profile_enable). */
+void ds3_cuda_profile_reset(void);
+void ds3_cuda_profile_print(const char *label);
+
+/* ------------------------------------------------------------------ */
+/* Fused ops (new). They replace the sequences named beside each.     */
+/* ------------------------------------------------------------------ */
+
+/* Token-embedding gather + dequant on the device. Replaces the CPU loop
+ * upload_token_embeddings (src/ds3_engine.c:273-290, ds3_ref_dequantize_row per
+ * token) plus the host->device copy. table: [n_vocab] rows of `row_stride`
+ * bytes of `type` (F32, F16, Q8_0, Q4_K, Q6_K); ids int32 [n_ids]; out fp32
+ * [n_ids, n_cols]. Bit-exact with the reference dequant. */
+int ds3_cuda_embed_rows(const ds3_cuda_buffer_t *table, const ds3_cuda_buffer_t *ids,
+                        ds3_cuda_buffer_t *out,
+                        uint32_t n_ids, uint32_t n_cols, uint32_t n_vocab,
+                        ds3_type_t type, uint64_t row_stride);
+
+/* Embedding gather + attn_norm RMSNorm in one pass: hidden_out gets the raw
+ * rows (the residual the engine keeps, src/ds3_engine.c:734), norm_out the
+ * normed rows (src/ds3_engine.c:744). hidden_out may be NULL. */
+int ds3_cuda_embed_rms_norm(const ds3_cuda_buffer_t *table, const ds3_cuda_buffer_t *ids,
+                            const ds3_cuda_buffer_t *weight,
+                            ds3_cuda_buffer_t *hidden_out, ds3_cuda_buffer_t *norm_out,
+                            uint32_t n_ids, uint32_t n_cols, uint32_t n_vocab,
+                            ds3_type_t type, uint64_t row_stride, float eps);
+
+/* Residual add + RMSNorm in one pass. Replaces vec_add_inplace + copy +
+ * rms_norm (src/ds3_engine.c:857-866). sum_out = x + residual (may be NULL,
+ * may alias x or residual); norm_out = rms_norm(sum) (may alias x). */
+int ds3_cuda_add_rms_norm(const ds3_cuda_buffer_t *x, const ds3_cuda_buffer_t *residual,
+                          const ds3_cuda_buffer_t *weight,
+                          ds3_cuda_buffer_t *sum_out, ds3_cuda_buffer_t *norm_out,
+                          uint32_t n, uint32_t n_rows, float eps);
+
+/* Per-head Q/K RMSNorm + NEOX RoPE, in place. Replaces the two per-head
+ * rms_norm calls (src/ds3_engine.c:789-792) and the per-token RoPE inside
+ * attention (src/ds3_metal.m:1241-1266). q [n_rows, n_q_heads, head_dim],
+ * k [n_rows, n_kv_heads, head_dim], stored as `storage` (DS3_TYPE_F32 or
+ * DS3_TYPE_F16; math is fp32 either way); q_w/k_w fp32 [head_dim]; positions
+ * int32 [n_rows]. k may be NULL when n_kv_heads == 0. */
+int ds3_cuda_qk_norm_rope(ds3_cuda_buffer_t *q, ds3_cuda_buffer_t *k,
+                          const ds3_cuda_buffer_t *q_w, const ds3_cuda_buffer_t *k_w,
+                          const ds3_cuda_buffer_t *positions,
+                          uint32_t n_rows, uint32_t n_q_heads, uint32_t n_kv_heads,
+                          uint32_t head_dim, float theta_base, float eps,
+                          ds3_type_t storage);
+
+/* Router softmax + top-k + renorm, one warp per token (the Metal kernel is
+ * one thread per token, metal/moe.metal:566-624). logits [n_tokens, n_expert];
+ * probs_out [n_tokens, n_expert] full softmax or NULL; idx int32 and scores
+ * fp32 [n_tokens, n_used], ordered by descending probability. */
+int ds3_cuda_router_softmax_topk(const ds3_cuda_buffer_t *logits,
+                                 ds3_cuda_buffer_t *probs_out,
+                                 ds3_cuda_buffer_t *idx, ds3_cuda_buffer_t *scores,
+                                 uint32_t n_tokens, uint32_t n_expert, uint32_t n_used,
+                                 bool norm_topk_prob);
+
+/* SwiGLU with optional per-row routing weight:
+ * out[r][c] = (silu(gate[r][c]) * up[r][c]) * row_weight[r]. row_weight may be
+ * NULL (plain silu_mul, metal/moe.metal:95-108). */
+int ds3_cuda_swiglu(const ds3_cuda_buffer_t *gate, const ds3_cuda_buffer_t *up,
+                    const ds3_cuda_buffer_t *row_weight, ds3_cuda_buffer_t *out,
+                    uint32_t n_rows, uint32_t n_cols);
+
+/* Weighted expert combine + residual. Replaces zero + per-expert
+ * scatter_add_weighted + vec_add (src/ds3_engine.c:1012-1019):
+ * out[t] = residual[t] + sum_k w[t,k] * y[row(t,k)], accumulated from zero in
+ * k order. row(t,k) = y_rows[t*n_used+k] (int32), or t*n_used+k when y_rows
+ * is NULL. out may alias residual. */
+int ds3_cuda_moe_combine_residual(const ds3_cuda_buffer_t *y, const ds3_cuda_buffer_t *y_rows,
+                                  const ds3_cuda_buffer_t *w, const ds3_cuda_buffer_t *residual,
+                                  ds3_cuda_buffer_t *out,
+                                  uint32_t n_tokens, uint32_t n_used, uint32_t n_cols);
+
+/* ------------------------------------------------------------------ */
+/* Streams, graphs, timers, errors (new)                              */
+/* ------------------------------------------------------------------ */
+
+/* The module stream (a cudaStream_t) all ops are enqueued on. */
+void *ds3_cuda_stream(void);
+
+/* Capture the ops enqueued between graph_begin and graph_end into a CUDA
+ * graph (ops only enqueue while capturing). graph_launch enqueues one replay
+ * without waiting; ds3_cuda_synchronize or end_batch waits. */
+typedef struct ds3_cuda_graph ds3_cuda_graph_t;
+int               ds3_cuda_graph_begin(void);
+ds3_cuda_graph_t *ds3_cuda_graph_end(void);
+int               ds3_cuda_graph_launch(ds3_cuda_graph_t *g);
+void              ds3_cuda_graph_free(ds3_cuda_graph_t *g);
+
+/* Event slots on the module stream (graph-capturable): mark(slot) records
+ * slot; elapsed_ms(a, b) waits for b and returns the time between them, or a
+ * negative value on error. Slots are 0 .. DS3_CUDA_TIMER_SLOTS-1. */
+#define DS3_CUDA_TIMER_SLOTS 16384
+int   ds3_cuda_timer_mark(int slot);
+float ds3_cuda_timer_elapsed_ms(int slot_a, int slot_b);
+
+/* Profiling switch (same effect as DS3_CUDA_PROFILE=1). */
+void ds3_cuda_profile_enable(int on);
+
+/* Last error message of this thread's calls ("" if none). */
+const char *ds3_cuda_last_error(void);
+
+/* Reads and clears the device error word (bit 0: bad token id; bit 1: a
+ * bounded wait ran out). Synchronises the module stream. */
+uint32_t ds3_cuda_device_errors(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DS3_CUDA_H */

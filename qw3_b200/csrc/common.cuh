@@ -1,0 +1,147 @@
+// Device helpers shared by the ds3_cuda kernels (sm_100a).
+//
+// Rounding discipline: where a kernel must reproduce the reference CPU
+// kernels bit for bit (dequant, residual add, combine) or within a few ulp
+// (norms, RoPE, softmax, SwiGLU), every multiply/add that the reference writes
+// as separate C operations is issued with an explicit round-to-nearest
+// intrinsic (__fmul_rn, __fadd_rn, __fsub_rn, __fdiv_rn, __fsqrt_rn). nvcc
+// never contracts those into an FMA, so the device performs the same roundings
+// in the same order as the reference's C code.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+namespace ds3 {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// Device error word, mapped from pinned host memory: kernels store 1 into a
+// slot (plain stores, no read-modify-write) and the host reads it after a
+// synchronisation. Slot meanings:
+enum : int { kErrBadId = 0, kErrWaitTimeout = 1, kErrSlots = 4 };
+
+__device__ __forceinline__ void flag_error(unsigned *err, int slot)
+{
+    if (err) *(volatile unsigned *)(err + slot) = 1u;
+}
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+    // Butterfly: lane i and lane i^o add the same two values, so every lane
+    // ends with the bit-identical total.
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+
+// 1 / sqrt(ss / n + eps), each step correctly rounded as in the reference
+// (ds3_reference.c: ss /= n; ss += eps; rms = 1.0f / sqrtf(ss)).
+__device__ __forceinline__ float rms_inv(float ss, int n, float eps)
+{
+    float m = __fdiv_rn(ss, (float)n);
+    m = __fadd_rn(m, eps);
+    return __fdiv_rn(1.0f, __fsqrt_rn(m));
+}
+
+// (x * inv) * w, left to right as the reference writes it.
+__device__ __forceinline__ float norm_mul(float x, float inv, float w)
+{
+    return __fmul_rn(__fmul_rn(x, inv), w);
+}
+
+__device__ __forceinline__ float sq_acc(float acc, float x) { return fmaf(x, x, acc); }
+
+__device__ __forceinline__ float4 f4_add(float4 a, float4 b)
+{
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y),
+                       __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+
+__device__ __forceinline__ float f4_sumsq(float4 v, float acc)
+{
+    acc = sq_acc(acc, v.x);
+    acc = sq_acc(acc, v.y);
+    acc = sq_acc(acc, v.z);
+    return sq_acc(acc, v.w);
+}
+
+__device__ __forceinline__ float4 f4_norm(float4 v, float inv, float4 w)
+{
+    return make_float4(norm_mul(v.x, inv, w.x), norm_mul(v.y, inv, w.y),
+                       norm_mul(v.z, inv, w.z), norm_mul(v.w, inv, w.w));
+}
+
+// Streaming (evict-first) 128-bit load for activations read exactly once.
+// These are coherent loads (ld.global.cs), so they stay correct for the
+// in-place calls where the same warp later writes the row it read.
+__device__ __forceinline__ float4 ld_stream(const float4 *p) { return __ldcs(p); }
+__device__ __forceinline__ float4 ld_param(const float4 *p) { return __ldg(p); }
+
+// ------------------------------------------------------------------------
+// mbarrier + bulk async copy (TMA, 1-D) helpers.
+// ------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void *p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// One bulk copy global -> shared (no multicast); completion is signalled on
+// `bar` as transaction bytes. dst/src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Bounded wait on an mbarrier phase. Returns false if the phase did not
+// complete within `limit` polls; the caller records the timeout and stops.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit)
+{
+    const uint32_t a = smem_addr(bar);
+    for (uint32_t it = 0; it < limit; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+}  // namespace ds3

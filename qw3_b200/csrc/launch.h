@@ -1,0 +1,55 @@
+// Internal launchers: raw device pointers + a stream. The C-ABI layer in
+// ds3_cuda.cu validates the public arguments, resolves buffers to pointers
+// and calls these. Each returns the launch status (cudaGetLastError).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace ds3 {
+
+struct LaunchCtx {
+    cudaStream_t stream;
+    unsigned *err;  // device-visible error word (see common.cuh)
+    int n_sm;
+};
+
+// x [rows, n] (+ r) -> sum_out (optional), norm_out. r == nullptr: plain RMSNorm.
+cudaError_t launch_add_rms_norm(const LaunchCtx &c, const float *x, const float *r, const float *w,
+                                float *sum_out, float *norm_out, int n, int64_t rows, float eps);
+
+// Embedding gather (+ RMSNorm when norm_out != nullptr).
+cudaError_t launch_embed(const LaunchCtx &c, const uint8_t *table, int type, uint64_t row_stride,
+                         int64_t n_vocab, const int32_t *ids, int64_t n_ids, int n_cols,
+                         float *hidden_out, const float *w, float *norm_out, float eps);
+
+// Per-head RMSNorm (when do_norm) + NEOX RoPE. storage: 0 = fp32, 1 = fp16.
+// q: [rows, nq, hd] read from q_src, written to q_dst (may alias); same for k.
+cudaError_t launch_qk_norm_rope(const LaunchCtx &c, const void *q_src, void *q_dst,
+                                const void *k_src, void *k_dst, const float *q_w,
+                                const float *k_w, const int32_t *pos, int64_t rows, int nq,
+                                int nk, int hd, const float *freq, float eps, int do_norm,
+                                int storage);
+
+cudaError_t launch_router_topk(const LaunchCtx &c, const float *logits, float *probs_out,
+                               int32_t *idx, float *scores, int64_t n_tokens, int n_expert,
+                               int n_used, int norm_topk);
+
+cudaError_t launch_swiglu(const LaunchCtx &c, const float *gate, const float *up,
+                          const float *row_w, float *out, int64_t rows, int64_t cols);
+
+cudaError_t launch_combine(const LaunchCtx &c, const float *y, const int32_t *y_rows,
+                           const float *w, const float *residual, float *out, int64_t n_tokens,
+                           int n_used, int64_t n_cols);
+
+cudaError_t launch_vec_add(const LaunchCtx &c, const float *a, const float *b, float *out,
+                           int64_t n);
+
+cudaError_t launch_gather_rows(const LaunchCtx &c, const float *src, const int32_t *ids,
+                               float *dst, int64_t n_cols, int64_t count, int64_t n_src_rows);
+
+cudaError_t launch_scatter_add_weighted(const LaunchCtx &c, const float *src, const float *scores,
+                                        const int32_t *ids, float *dst, int64_t n_cols,
+                                        int64_t count, int64_t n_dst_rows);
+
+}  // namespace ds3

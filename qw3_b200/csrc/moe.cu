@@ -1,0 +1,266 @@
+// Routed-expert elementwise kernels and the small FP32 helpers (sm_100a):
+// SwiGLU (optionally weighted), weighted combine + residual, vec_add,
+// gather/scatter of rows.
+//
+// References: ds3_ref_silu / ds3_ref_mul (src/ds3_reference.c:436-448),
+// moe_expert_silu_mul_f32 (metal/moe.metal:95-108); the weighted expert
+// accumulation and residual add of ds3_ref_moe_ffn / ds3_ref_layer_forward
+// (src/ds3_reference.c:642, :674-678, :777); vec_add / gather_rows /
+// scatter_add_weighted (metal/elementwise.metal:146-211).
+//
+// All are streaming kernels: 128-bit loads/stores, several independent
+// 16-byte loads in flight per thread, grids sized to fill the 148 SMs.
+#include "common.cuh"
+#include "launch.h"
+
+namespace ds3 {
+namespace {
+
+bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+__device__ __forceinline__ float silu_mul(float g, float u)
+{
+    // (g / (1 + expf(-g))) * u, each step rounded as the reference's C.
+    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    return __fmul_rn(s, u);
+}
+
+// ------------------------------------------------------------------ SwiGLU
+constexpr int kSwigluUnroll = 4;
+
+__global__ void __launch_bounds__(256) swiglu_vec(const float4 *gate, const float4 *up,
+                                                  const float *row_w, float4 *out, int64_t units,
+                                                  int64_t cols4)
+{
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    int64_t u0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; u0 < units; u0 += stride * kSwigluUnroll) {
+        float4 g[kSwigluUnroll], v[kSwigluUnroll];
+#pragma unroll
+        for (int k = 0; k < kSwigluUnroll; k++) {
+            const int64_t u = u0 + k * stride;
+            if (u < units) {
+                g[k] = ld_stream(gate + u);
+                v[k] = ld_stream(up + u);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kSwigluUnroll; k++) {
+            const int64_t u = u0 + k * stride;
+            if (u >= units) break;
+            float4 o = make_float4(silu_mul(g[k].x, v[k].x), silu_mul(g[k].y, v[k].y),
+                                   silu_mul(g[k].z, v[k].z), silu_mul(g[k].w, v[k].w));
+            if (row_w) {
+                const float w = __ldg(row_w + u / cols4);
+                o = make_float4(__fmul_rn(o.x, w), __fmul_rn(o.y, w), __fmul_rn(o.z, w), __fmul_rn(o.w, w));
+            }
+            out[u] = o;
+        }
+    }
+}
+
+__global__ void swiglu_scalar(const float *gate, const float *up, const float *row_w, float *out,
+                              int64_t n, int64_t cols)
+{
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float o = silu_mul(gate[i], up[i]);
+        if (row_w) o = __fmul_rn(o, row_w[i / cols]);
+        out[i] = o;
+    }
+}
+
+// --------------------------------------------------------- combine + residual
+// One thread per (token, float4 column): all n_used expert rows of that
+// column are loaded before the sum, which runs from zero in k order.
+template <int K>
+__global__ void __launch_bounds__(128) combine_vec(const float4 *y, const int32_t *y_rows,
+                                                   const float *w, const float4 *residual,
+                                                   float4 *out, int64_t n_tokens, int n_used,
+                                                   int64_t cols4)
+{
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n_tokens * cols4) return;
+    const int64_t t = e / cols4;
+    const int64_t c = e - t * cols4;
+    const int nk = K > 0 ? K : n_used;
+    const float4 res = ld_stream(residual + e);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (K > 0) {
+        float4 yv[K];
+        float wk[K];
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+            const int64_t r = y_rows ? (int64_t)y_rows[t * K + k] : t * K + k;
+            yv[k] = ld_stream(y + r * cols4 + c);
+            wk[k] = __ldg(w + t * K + k);
+        }
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+            acc.x = __fadd_rn(acc.x, __fmul_rn(wk[k], yv[k].x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(wk[k], yv[k].y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(wk[k], yv[k].z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(wk[k], yv[k].w));
+        }
+    } else {
+        for (int k = 0; k < nk; k++) {
+            const int64_t r = y_rows ? (int64_t)y_rows[t * nk + k] : t * nk + k;
+            const float4 yv = ld_stream(y + r * cols4 + c);
+            const float wk = __ldg(w + t * nk + k);
+            acc.x = __fadd_rn(acc.x, __fmul_rn(wk, yv.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(wk, yv.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(wk, yv.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(wk, yv.w));
+        }
+    }
+    out[e] = f4_add(res, acc);
+}
+
+__global__ void combine_scalar(const float *y, const int32_t *y_rows, const float *w,
+                               const float *residual, float *out, int64_t n_tokens, int n_used,
+                               int64_t cols)
+{
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_tokens * cols;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = e / cols, c = e - t * cols;
+        float acc = 0.0f;
+        for (int k = 0; k < n_used; k++) {
+            const int64_t r = y_rows ? (int64_t)y_rows[t * n_used + k] : t * n_used + k;
+            acc = __fadd_rn(acc, __fmul_rn(w[t * n_used + k], y[r * cols + c]));
+        }
+        out[e] = __fadd_rn(residual[e], acc);
+    }
+}
+
+// ----------------------------------------------------------------- vec_add
+__global__ void vec_add_vec(const float4 *a, const float4 *b, float4 *c, int64_t n4)
+{
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += (int64_t)gridDim.x * blockDim.x)
+        c[i] = f4_add(ld_stream(a + i), ld_stream(b + i));
+}
+
+__global__ void vec_add_scalar(const float *a, const float *b, float *c, int64_t n)
+{
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        c[i] = __fadd_rn(a[i], b[i]);
+}
+
+// ------------------------------------------------------- gather / scatter
+__global__ void gather_rows_k(const float *src, const int32_t *ids, float *dst, int64_t n_cols,
+                              int64_t count, int64_t n_src_rows, unsigned *err)
+{
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < count * n_cols;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = e / n_cols, j = e - i * n_cols;
+        const int64_t r = ids[i];
+        if (r < 0 || r >= n_src_rows) {
+            if (j == 0) flag_error(err, kErrBadId);
+            dst[e] = 0.0f;
+            continue;
+        }
+        dst[e] = src[r * n_cols + j];
+    }
+}
+
+__global__ void scatter_add_k(const float *src, const float *scores, const int32_t *ids, float *dst,
+                              int64_t n_cols, int64_t count, int64_t n_dst_rows, unsigned *err)
+{
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < count * n_cols;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = e / n_cols, j = e - i * n_cols;
+        const int64_t r = ids[i];
+        if (r < 0 || r >= n_dst_rows) {
+            if (j == 0) flag_error(err, kErrBadId);
+            continue;
+        }
+        float *d = dst + r * n_cols + j;
+        *d = __fadd_rn(*d, __fmul_rn(scores[i], src[e]));
+    }
+}
+
+unsigned grid_for(const LaunchCtx &c, int64_t work, int threads, int per_sm)
+{
+    int64_t b = (work + threads - 1) / threads;
+    const int64_t cap = (int64_t)c.n_sm * per_sm;
+    if (b > cap) b = cap;
+    if (b < 1) b = 1;
+    return (unsigned)b;
+}
+
+}  // namespace
+
+cudaError_t launch_swiglu(const LaunchCtx &c, const float *gate, const float *up,
+                          const float *row_w, float *out, int64_t rows, int64_t cols)
+{
+    const int64_t n = rows * cols;
+    if (n <= 0) return cudaSuccess;
+    if (cols % 4 == 0 && al16(gate) && al16(up) && al16(out)) {
+        const int64_t units = n / 4;
+        // Enough threads for ~4 x 2 x 16 B in flight each across all SMs.
+        const unsigned blocks = grid_for(c, (units + kSwigluUnroll - 1) / kSwigluUnroll, 256, 8);
+        swiglu_vec<<<blocks, 256, 0, c.stream>>>(reinterpret_cast<const float4 *>(gate),
+                                                 reinterpret_cast<const float4 *>(up), row_w,
+                                                 reinterpret_cast<float4 *>(out), units, cols / 4);
+    } else {
+        swiglu_scalar<<<grid_for(c, n, 256, 16), 256, 0, c.stream>>>(gate, up, row_w, out, n, cols);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const LaunchCtx &c, const float *y, const int32_t *y_rows,
+                           const float *w, const float *residual, float *out, int64_t n_tokens,
+                           int n_used, int64_t n_cols)
+{
+    if (n_tokens <= 0 || n_cols <= 0) return cudaSuccess;
+    if (n_cols % 4 == 0 && al16(y) && al16(residual) && al16(out)) {
+        const int64_t cols4 = n_cols / 4;
+        const int64_t total = n_tokens * cols4;
+        const unsigned blocks = (unsigned)((total + 127) / 128);
+        auto *y4 = reinterpret_cast<const float4 *>(y);
+        auto *r4 = reinterpret_cast<const float4 *>(residual);
+        auto *o4 = reinterpret_cast<float4 *>(out);
+        if (n_used == 8)
+            combine_vec<8><<<blocks, 128, 0, c.stream>>>(y4, y_rows, w, r4, o4, n_tokens, n_used, cols4);
+        else
+            combine_vec<0><<<blocks, 128, 0, c.stream>>>(y4, y_rows, w, r4, o4, n_tokens, n_used, cols4);
+    } else {
+        combine_scalar<<<grid_for(c, n_tokens * n_cols, 256, 16), 256, 0, c.stream>>>(
+            y, y_rows, w, residual, out, n_tokens, n_used, n_cols);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_vec_add(const LaunchCtx &c, const float *a, const float *b, float *out, int64_t n)
+{
+    if (n <= 0) return cudaSuccess;
+    if (n % 4 == 0 && al16(a) && al16(b) && al16(out))
+        vec_add_vec<<<grid_for(c, n / 4, 256, 16), 256, 0, c.stream>>>(
+            reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b),
+            reinterpret_cast<float4 *>(out), n / 4);
+    else
+        vec_add_scalar<<<grid_for(c, n, 256, 16), 256, 0, c.stream>>>(a, b, out, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const LaunchCtx &c, const float *src, const int32_t *ids,
+                               float *dst, int64_t n_cols, int64_t count, int64_t n_src_rows)
+{
+    if (count <= 0 || n_cols <= 0) return cudaSuccess;
+    gather_rows_k<<<grid_for(c, count * n_cols, 256, 16), 256, 0, c.stream>>>(src, ids, dst, n_cols, count,
+                                                                             n_src_rows, c.err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_add_weighted(const LaunchCtx &c, const float *src, const float *scores,
+                                        const int32_t *ids, float *dst, int64_t n_cols,
+                                        int64_t count, int64_t n_dst_rows)
+{
+    if (count <= 0 || n_cols <= 0) return cudaSuccess;
+    scatter_add_k<<<grid_for(c, count * n_cols, 256, 16), 256, 0, c.stream>>>(
+        src, scores, ids, dst, n_cols, count, n_dst_rows, c.err);
+    return cudaGetLastError();
+}
+
+}  // namespace ds3
