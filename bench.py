@@ -1,0 +1,755 @@
+"""Benchmark of the fused per-layer path (one JSON line on rank 0).
+
+Metric: fused-layer tokens/s/GPU at T=512, and HBM GB/s as a
+fraction of 8 TB/s, on 1/2/4/8 B200.
+
+A "step" is one pass of the hot path over one 512-token prefill chunk per GPU
+(the engine's chunk size, src/ds3.h:82), through the ds3_cuda C-ABI:
+  1. embed_rms_norm        Q4_K token_embd gather + dequant + attn_norm
+  2. qk_norm_rope          per-head Q/K RMSNorm + NEOX RoPE (32 Q / 4 KV heads)
+  3. add_rms_norm          residual add + ffn_norm
+  4. router_softmax_topk   softmax over 128 experts, top-8, renorm
+  5. swiglu                silu(gate)*up * routing weight, 4096 x 768
+  6. moe_combine_residual  weighted sum of 8 expert rows + residual
+The projections between these ops (QKV/O, router logits, expert matmuls) are
+out of scope; their outputs are seeded synthetic tensors of the right shapes.
+Scaling is weak: every GPU runs its own 512-token chunk, with no collective.
+
+value   : whole-job tokens/s, inputs resident in HBM (K graph replays, CUDA
+          events on the module stream, barrier + synchronize both sides, max
+          over ranks). Inputs rotate over several sets larger than L2 together.
+e2e     : same step through the C-ABI from pinned host buffers, host->device
+          copies of every input and device->host read of the outputs timed.
+roofline: the kernel with the largest share of the step, algorithmic bytes per
+          launch / its average CUDA-event duration, against the measured HBM
+          copy peak.
+--impl reference: the reference's own CPU kernels (oracle/_ref, the unmodified
+          src/ds3_reference.c) on the same workload, all host threads, rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from qw3_b200 import inputs as I  # noqa: E402
+
+METRIC = "fused-layer tokens/s/GPU at T=512 and HBM GB/s as % of 8 TB/s, 1/2/4/8 B200"
+T = 512
+H = I.N_EMBD
+NQ, NK, HD = I.N_HEAD, I.N_HEAD_KV, I.HEAD_DIM
+E, K = I.N_EXPERT, I.N_EXPERT_USED
+FF = I.N_FF_EXP
+V = I.N_VOCAB
+Q4K_ROW = H // 256 * 144
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+# Algorithmic bytes per launch (per 512-token chunk): what each op must read
+# and write at least once. Shared parameters (gammas, frequency table) are
+# not counted; only the gathered embedding rows are.
+ALGO_BYTES = {
+    "embed_rms_norm": T * (Q4K_ROW + 4 + 4 * H + 4 * H),
+    "qk_norm_rope": T * (2 * 4 * (NQ + NK) * HD + 4),
+    "add_rms_norm": T * 4 * H * 4,
+    "router_softmax_topk": T * (4 * E + 4 * K + 4 * K),
+    "swiglu": T * K * (3 * 4 * FF + 4),
+    "moe_combine_residual": T * (K * 4 * H + 4 * H + 4 * K + 4 * H),
+}
+OPS = list(ALGO_BYTES)
+STEP_BYTES = sum(ALGO_BYTES.values())
+
+# DRAM traffic per launch measured with ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum, --clock-control none) on this workload; None where
+# no capture exists yet.
+NCU_TRAFFIC = {}
+
+CONFIG = {
+    "workload": "fused_layer_T512",
+    "tokens_per_gpu": T,
+    "ops": OPS,
+    "table": "Q4_K token_embd 151936x2048 (175 MB, device-resident)",
+    "model_dims": "Qwen3-30B-A3B: n_embd 2048, 32 Q / 4 KV heads x 128, 128 experts top-8, n_ff_exp 768",
+    "parallelism": "row shard, one 512-token chunk per GPU, no collective",
+}
+
+
+# --------------------------------------------------------------------------
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def make_host_set(seed: int, table_rows: int = V):
+    """One step's inputs (numpy, host) for a 512-token chunk."""
+    g = {}
+    g["ids"] = I.token_ids(T, seed + 0, table_rows)
+    g["pos"] = np.arange(T, dtype=np.int32)
+    g["q"] = I.normal(seed + 1, (T, NQ, HD))
+    g["k"] = I.normal(seed + 2, (T, NK, HD))
+    g["attn_out"] = I.normal(seed + 3, (T, H))
+    g["logits"] = I.normal(seed + 4, (T, E), 0.0, 2.0)
+    g["gate"] = I.normal(seed + 5, (T * K, FF), 0.0, 1.5)
+    g["up"] = I.normal(seed + 6, (T * K, FF), 0.0, 1.5)
+    g["y"] = I.normal(seed + 7, (T * K, H))
+    return g
+
+
+def make_params():
+    return {
+        "attn_norm": I.gamma(H, 1101),
+        "ffn_norm": I.gamma(H, 1102),
+        "q_norm": I.gamma(HD, 1103),
+        "k_norm": I.gamma(HD, 1104),
+    }
+
+
+class DevSet:
+    """Device buffers for one step (inputs + outputs)."""
+
+    IN = ["ids", "pos", "q", "k", "attn_out", "logits", "gate", "up", "y"]
+
+    def __init__(self, ds3, host):
+        self.b = {n: ds3.upload(host[n]) for n in self.IN}
+        for n, nbytes in (("hidden", T * H * 4), ("xnorm", T * H * 4), ("resid", T * H * 4),
+                          ("ffn_in", T * H * 4), ("idx", T * K * 4), ("scores", T * K * 4),
+                          ("act", T * K * FF * 4), ("out", T * H * 4)):
+            self.b[n] = ds3.empty(nbytes)
+
+    def free(self):
+        for b in self.b.values():
+            b.free()
+
+
+def enqueue_step(ds3, P, S, marks=None):
+    """Enqueue the six ops of one step; with `marks` (list of timer slots),
+    record a timer event before the first op and after every op."""
+    b = S.b
+    eps = I.NORM_EPS
+
+    def mark(i):
+        if marks is not None:
+            ds3.timer_mark(marks[i])
+
+    mark(0)
+    rc = ds3.embed_rms_norm(P["table"], b["ids"], P["attn_norm"], b["hidden"], b["xnorm"], T, H, V,
+                            ds3.TYPE_Q4_K, Q4K_ROW, eps)
+    mark(1)
+    rc |= ds3.qk_norm_rope(b["q"], b["k"], P["q_norm"], P["k_norm"], b["pos"], T, NQ, NK, HD, I.ROPE_THETA, eps)
+    mark(2)
+    rc |= ds3.add_rms_norm(b["attn_out"], b["hidden"], P["ffn_norm"], b["resid"], b["ffn_in"], H, T, eps)
+    mark(3)
+    rc |= ds3.router_softmax_topk(b["logits"], None, b["idx"], b["scores"], T, E, K, True)
+    mark(4)
+    rc |= ds3.swiglu(b["gate"], b["up"], b["scores"], b["act"], T * K, FF)
+    mark(5)
+    rc |= ds3.moe_combine_residual(b["y"], None, b["scores"], b["resid"], b["out"], T, K, H)
+    mark(6)
+    if rc != 0:
+        raise RuntimeError("enqueue failed: " + ds3.last_error())
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples, self.reasons = [], 0
+        self.max_mhz = None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML unavailable: report nothing rather than guess
+            self.nv = None
+
+    def _sample(self):
+        self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+        try:
+            self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            self.reasons |= self.nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def start(self):
+        if self.nv:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self._t:
+            self._stop.set()
+            self._t.join()
+            if not self.samples:
+                self._sample()
+
+    def summary(self):
+        if not self.nv or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            v = float(json.loads(p.read_text())["hbm_gbs"])
+            return v, "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------ CPU reference
+def cpu_oracle():
+    import oracle
+
+    oracle.build() if not oracle.PORT_LIB.exists() else None
+    ref = oracle.reference()
+    if ref is not None:
+        return ref, "reference"
+    return oracle.port(), "port"
+
+
+def cpu_step(O, table, params, g, n_tok, threads):
+    """The same six ops on the host CPU for the first n_tok tokens of set g."""
+    eps = I.NORM_EPS
+    ids = g["ids"][:n_tok]
+    _, hid, _ = O.embed_rms_norm(table, 12, Q4K_ROW, V, ids, H, params["attn_norm"], eps, threads)
+    O.qk_norm_rope(g["q"][:n_tok], g["k"][:n_tok], params["q_norm"], params["k_norm"], g["pos"][:n_tok],
+                   I.ROPE_THETA, eps, threads)
+    s, _ = O.add_rms_norm(g["attn_out"][:n_tok], hid, params["ffn_norm"], eps, threads)
+    _, _, sc = O.router(g["logits"][:n_tok], K, True, threads)
+    O.swiglu(g["gate"][: n_tok * K], g["up"][: n_tok * K], sc.reshape(-1), threads)
+    O.combine(g["y"][: n_tok * K], sc, s, None, threads)
+
+
+def time_cpu(O, table, params, g, threads, budget_s=10.0, max_steps=None):
+    """Tokens/s of the CPU path on a bounded sample: whole 512-token steps
+    until `budget_s` is spent (at least one); sub-chunks if one step is
+    longer than the budget."""
+    t0 = time.perf_counter()
+    cpu_step(O, table, params, g, 32, threads)  # warm caches / threads
+    probe = time.perf_counter() - t0
+    n_tok = T if probe * (T / 32) <= budget_s else max(8, int(32 * budget_s / max(probe, 1e-9) / 4))
+    steps, tok = 0, 0
+    t0 = time.perf_counter()
+    while True:
+        cpu_step(O, table, params, g, n_tok, threads)
+        steps += 1
+        tok += n_tok
+        el = time.perf_counter() - t0
+        if el >= budget_s or (max_steps and steps >= max_steps):
+            break
+    return tok / el, {"tokens": tok, "steps": steps, "tokens_per_step": n_tok, "seconds": round(el, 3)}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    O, kind = cpu_oracle()
+    threads = cpu_cores()
+    table = I.q4k_table(V, H, 1)
+    params = make_params()
+    g = make_host_set(seed=2000)
+    # One untimed step sizes the sample so K steps end within ~2 minutes.
+    t0 = time.perf_counter()
+    cpu_step(O, table, params, g, T, threads)
+    full = time.perf_counter() - t0
+    n_tok = T
+    budget = 120.0
+    if full * (args.steps + args.warmup) > budget:
+        n_tok = max(8, int(T * budget / (full * (args.steps + args.warmup))))
+    for _ in range(args.warmup):
+        cpu_step(O, table, params, g, n_tok, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(O, table, params, g, n_tok, threads)
+    el = time.perf_counter() - t0
+    value = n_tok * args.steps / el
+    sample = f"{n_tok} of {T} tokens per step, {args.steps} steps, {el:.2f} s"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * el / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; no dataset or weights exist for this path)", "config": CONFIG,
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "hbm_gbs_per_gpu": None,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--sets", type=int, default=4, help="input sets rotated to defeat L2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the per-config kernel lines")
+    ap.add_argument("--profile", action="store_true", help="short run for ncu: no e2e, baseline or configs")
+    ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between ops (1/0)")
+    args = ap.parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    os.environ["DS3_CUDA_PDL"] = str(args.pdl)
+    from qw3_b200 import ds3
+
+    if ds3.set_device(local) != 0 or ds3.init() != 0:
+        raise SystemExit("ds3_cuda_init failed: " + ds3.last_error())
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- inputs: table shared by all steps, S rotating sets of activations
+    table_host = I.q4k_table(V, H, 1)
+    params_host = make_params()
+    P = {"table": ds3.buffer_from_mmap(table_host)}
+    for n, a in params_host.items():
+        P[n] = ds3.upload(a)
+    hosts = [make_host_set(seed=2000 + 97 * s + 10007 * rank) for s in range(args.sets)]
+    sets = [DevSet(ds3, h) for h in hosts]
+
+    # ---- parity check of one step (set 0) against the oracle before timing
+    import oracle
+
+    O = oracle.port()
+    enqueue_step(ds3, P, sets[0])
+    ds3.synchronize()
+    parity = check_step(ds3, O, table_host, params_host, hosts[0], sets[0])
+    # restore the in-place Q/K of set 0
+    ds3.buffer_write(sets[0].b["q"], 0, hosts[0]["q"])
+    ds3.buffer_write(sets[0].b["k"], 0, hosts[0]["k"])
+
+    # ---- graphs: one per input set
+    graphs = []
+    for S in sets:
+        ds3.graph_begin()
+        enqueue_step(ds3, P, S)
+        graphs.append(ds3.graph_end())
+
+    for i in range(args.warmup):
+        ds3.graph_launch(graphs[i % len(graphs)])
+    ds3.synchronize()
+
+    clocks = ClockSampler(local)
+    barrier()
+    ds3.synchronize()
+    clocks.start()
+    ds3.timer_mark(0)
+    for i in range(args.steps):
+        ds3.graph_launch(graphs[i % len(graphs)])
+    ds3.timer_mark(1)
+    ds3.synchronize()
+    clocks.stop()
+    barrier()
+    ms = ds3.timer_elapsed_ms(0, 1)
+    ms = max_over_ranks(ms)
+    ms_step = ms / args.steps
+    value = world * T / (ms_step * 1e-3)
+
+    # ---- per-kernel durations: each op alone, back to back, over copies of
+    # its operands that together exceed L2 (so every launch streams from HBM)
+    peak, peak_kind = measured_peak()
+    kernels = op_loops(ds3, P, max_over_ranks, barrier, peak)
+    tot = sum(k["avg_us"] for k in kernels.values())
+    for k in kernels.values():
+        k["share"] = round(k["avg_us"] / tot, 4)
+    dom = max(kernels, key=lambda o: kernels[o]["avg_us"])
+    d = kernels[dom]
+    roofline = {"kernel": dom, "bound": "hbm", "achieved": d["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": round(d["gbs"] / peak, 4), "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                "traffic": NCU_TRAFFIC.get(dom), "algo_bytes_per_launch": ALGO_BYTES[dom],
+                "timing": "CUDA events around back-to-back launches of this kernel alone (graph, module stream)"}
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; no dataset or weights exist for this path)",
+        "config": dict(CONFIG, global_tokens=world * T, pdl=bool(args.pdl),
+                       l2="inputs rotate over %d sets (%.0f MB each, %.0f MB total > 126 MB L2) plus a 175 MB table"
+                          % (len(sets), set_bytes(hosts[0]) / 1e6, len(sets) * set_bytes(hosts[0]) / 1e6)),
+        "hbm_gbs_per_gpu": round(STEP_BYTES / (ms_step * 1e-3) / 1e9, 1),
+        "pct_of_8tbs": round(100 * STEP_BYTES / (ms_step * 1e-3) / 1e9 / NOMINAL_HBM_GBS, 2),
+        "pct_of_measured_peak": round(100 * STEP_BYTES / (ms_step * 1e-3) / 1e9 / peak, 2),
+        "step_algo_bytes": STEP_BYTES,
+        "roofline": roofline,
+        "kernels": kernels,
+        "gpu_launches": 6 * args.steps,
+        "clocks": clocks.summary(),
+        "parity": parity,
+    }
+
+    if not args.profile:
+        line["e2e"] = run_e2e(ds3, P, sets[0], hosts[0], args.steps, world, max_over_ranks, barrier)
+        if not args.no_configs:
+            line["configs"] = run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_host)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            Oc, kind = cpu_oracle()
+            thr = cpu_cores()
+            v, sample = time_cpu(Oc, table_host, params_host, hosts[0], thr)
+            line["cpu_baseline"] = {"value": round(v, 2), "unit": "tokens/s", "cores": thr, "kind": kind,
+                                    "sample": f"{sample['steps']} steps x {sample['tokens_per_step']} tokens of "
+                                              f"the same workload in {sample['seconds']} s"}
+    for g in graphs:
+        ds3.graph_free(g)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def set_bytes(h):
+    return sum(a.nbytes for a in h.values())
+
+
+def check_step(ds3, O, table, params, g, S):
+    """Compare one device step with the oracle (exact where the path is exact)."""
+    eps = I.NORM_EPS
+    b = S.b
+    res = {}
+    _, hid, xn = O.embed_rms_norm(table, 12, Q4K_ROW, V, g["ids"], H, params["attn_norm"], eps, 8)
+    got = ds3.download(b["hidden"], np.float32, (T, H))
+    res["embed_bitexact"] = bool(np.array_equal(got.view(np.uint32), hid.view(np.uint32)))
+    qo, ko = O.qk_norm_rope(g["q"], g["k"], params["q_norm"], params["k_norm"], g["pos"], I.ROPE_THETA, eps, 8)
+    gq = ds3.download(b["q"], np.float32, qo.shape)
+    # worst |err| / (1e-6 + 1e-5 |want|): <= 1 means within the stated tolerance
+    res["qk_rope_tol_ratio"] = float(np.max(np.abs(gq - qo) / (1e-6 + 1e-5 * np.abs(qo))))
+    s, _ = O.add_rms_norm(g["attn_out"], hid, params["ffn_norm"], eps, 8)
+    res["residual_bitexact"] = bool(np.array_equal(ds3.download(b["resid"], np.float32, (T, H)), s))
+    _, idx, _ = O.router(g["logits"], K, True, 8)
+    res["top8_exact"] = bool(np.array_equal(ds3.download(b["idx"], np.int32, (T, K)), idx))
+    w = ds3.download(b["scores"], np.float32, (T, K))
+    out = O.combine(g["y"], w, s, None, 8)
+    res["combine_bitexact"] = bool(np.array_equal(ds3.download(b["out"], np.float32, (T, H)), out))
+    return res
+
+
+def op_loops(ds3, P, max_over_ranks, barrier, peak, budget=320e6):
+    """Average duration of each op of the step launched alone, back to back,
+    rotating over n copies of its activations (n * bytes >= budget > L2).
+    Copies are slices of framework-allocated device slabs (random fill on the
+    device), wrapped as ds3_cuda buffers."""
+    import math
+
+    import torch
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)
+    out = {}
+    keep = []
+
+    def slab(shape, kind="normal", std=1.0, hi=V):
+        if kind == "normal":
+            t = torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * std
+        elif kind == "ids":
+            t = torch.randint(0, hi, shape, generator=gen, device=dev, dtype=torch.int32)
+        elif kind == "uniform":
+            t = torch.rand(shape, generator=gen, device=dev, dtype=torch.float32)
+        else:
+            t = torch.empty(shape, device=dev, dtype=torch.float32)
+        keep.append(t)
+        return t
+
+    def views(t, n):
+        w = ds3.buffer_wrap(t.data_ptr(), t.numel() * t.element_size())
+        keep.append(w)
+        per = t.numel() * t.element_size() // n
+        vs = [ds3.buffer_view(w, i * per, per) for i in range(n)]
+        keep.extend(vs)
+        return vs
+
+    eps = I.NORM_EPS
+    for op in OPS:
+        n = int(min(2048, max(2, math.ceil(budget / ALGO_BYTES[op]))))
+        if op == "embed_rms_norm":
+            ids, hid, nrm = views(slab((n, T), "ids"), n), views(slab((n, T, H), "empty"), n), views(
+                slab((n, T, H), "empty"), n)
+            fns = [lambda i=i: ds3.embed_rms_norm(P["table"], ids[i], P["attn_norm"], hid[i], nrm[i], T, H, V,
+                                                  ds3.TYPE_Q4_K, Q4K_ROW, eps) for i in range(n)]
+        elif op == "qk_norm_rope":
+            q, k = views(slab((n, T, NQ, HD)), n), views(slab((n, T, NK, HD)), n)
+            pos = views(slab((n, T), "ids", hi=T), n)
+            fns = [lambda i=i: ds3.qk_norm_rope(q[i], k[i], P["q_norm"], P["k_norm"], pos[i], T, NQ, NK, HD,
+                                                I.ROPE_THETA, eps) for i in range(n)]
+        elif op == "add_rms_norm":
+            x, r = views(slab((n, T, H)), n), views(slab((n, T, H)), n)
+            so, no = views(slab((n, T, H), "empty"), n), views(slab((n, T, H), "empty"), n)
+            fns = [lambda i=i: ds3.add_rms_norm(x[i], r[i], P["ffn_norm"], so[i], no[i], H, T, eps) for i in range(n)]
+        elif op == "router_softmax_topk":
+            lg = views(slab((n, T, E), std=2.0), n)
+            ix, sc = views(slab((n, T, K), "empty"), n), views(slab((n, T, K), "empty"), n)
+            fns = [lambda i=i: ds3.router_softmax_topk(lg[i], None, ix[i], sc[i], T, E, K, True) for i in range(n)]
+        elif op == "swiglu":
+            g, u = views(slab((n, T * K, FF), std=1.5), n), views(slab((n, T * K, FF), std=1.5), n)
+            w, o = views(slab((n, T * K), "uniform"), n), views(slab((n, T * K, FF), "empty"), n)
+            fns = [lambda i=i: ds3.swiglu(g[i], u[i], w[i], o[i], T * K, FF) for i in range(n)]
+        else:
+            y, r = views(slab((n, T * K, H)), n), views(slab((n, T, H)), n)
+            w, o = views(slab((n, T, K), "uniform"), n), views(slab((n, T, H), "empty"), n)
+            fns = [lambda i=i: ds3.moe_combine_residual(y[i], None, w[i], r[i], o[i], T, K, H) for i in range(n)]
+        torch.cuda.synchronize()
+        reps = max(n, 64)
+        ms = time_launches(ds3, fns, reps, max_over_ranks, barrier)
+        gbs = ALGO_BYTES[op] / (ms * 1e-3) / 1e9
+        out[op] = {"avg_us": round(ms * 1e3, 3), "algo_bytes": ALGO_BYTES[op], "gbs": round(gbs, 1),
+                   "frac_of_measured_peak": round(gbs / peak, 4), "copies": n}
+        for x in keep:
+            if hasattr(x, "free"):
+                x.free()
+        keep.clear()
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_e2e(ds3, P, S, host, steps, world, max_over_ranks, barrier):
+    """Same step from pinned host memory: every input is copied host->device
+    and the step's outputs read back, inside the timed region."""
+    import torch
+
+    def pinned(a):
+        t = torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+        return t.numpy()
+
+    src = {n: pinned(host[n]) for n in DevSet.IN}
+    outs = {"out": np.empty((T, H), np.float32), "idx": np.empty((T, K), np.int32),
+            "scores": np.empty((T, K), np.float32)}
+    outs = {n: pinned(a) for n, a in outs.items()}
+    h2d = sum(a.nbytes for a in src.values())
+    d2h = sum(a.nbytes for a in outs.values())
+    n = max(3, min(steps, 200))
+
+    def one():
+        for name, a in src.items():
+            if ds3.buffer_write(S.b[name], 0, a) != 0:
+                raise RuntimeError(ds3.last_error())
+        ds3.begin_batch()
+        enqueue_step(ds3, P, S)
+        if ds3.end_batch() != 0:
+            raise RuntimeError(ds3.last_error())
+        for name, a in outs.items():
+            if ds3.buffer_read(S.b[name], 0, a) != 0:
+                raise RuntimeError(ds3.last_error())
+
+    for _ in range(3):
+        one()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(n):
+        one()
+    el = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    return {"value": round(world * T * n / el, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(1e3 * el / n, 4),
+            "api": "ds3_cuda_buffer_write / begin_batch / 6 ops / end_batch / buffer_read (wall clock)"}
+
+
+# ------------------------------------------------------ per-config kernels
+def time_launches(ds3, fns, reps, max_over_ranks, barrier):
+    """Average device time of fns[i % len(fns)]() over `reps` launches, with
+    warm-up, captured in one graph and timed with events on the module stream."""
+    for i in range(3):
+        fns[i % len(fns)]()
+    ds3.synchronize()
+    ds3.graph_begin()
+    for i in range(reps):
+        fns[i % len(fns)]()
+    g = ds3.graph_end()
+    ds3.graph_launch(g)
+    ds3.synchronize()
+    barrier()
+    ds3.timer_mark(2)
+    ds3.graph_launch(g)
+    ds3.timer_mark(3)
+    ds3.synchronize()
+    ms = max_over_ranks(ds3.timer_elapsed_ms(2, 3)) / reps
+    ds3.graph_free(g)
+    return ms
+
+
+def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k):
+    """Kernel throughput on BASELINE configs 2-5 (per GPU; C4/C5 rows sharded
+    across the ranks). Inputs rotate over buffers larger than L2."""
+    from qw3_b200.shard import shard_range
+
+    out = {}
+    eps = I.NORM_EPS
+    bufs = []
+
+    def up(a):
+        b = ds3.upload(a)
+        bufs.append(b)
+        return b
+
+    def empty(n):
+        b = ds3.empty(n)
+        bufs.append(b)
+        return b
+
+    def rec(name, tokens, nbytes, ms, note=""):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"tokens_per_s": round(tokens * world / (ms * 1e-3), 1), "us": round(ms * 1e3, 3),
+                     "algo_bytes": nbytes, "gbs_per_gpu": round(gbs, 1),
+                     "pct_of_8tbs": round(100 * gbs / NOMINAL_HBM_GBS, 2),
+                     "frac_of_measured_peak": round(gbs / peak, 4)}
+        if note:
+            out[name]["note"] = note
+
+    # C4: add + RMSNorm on [32768, 2048], rows sharded; 2 buffer sets (1 GB each).
+    a, b = shard_range(32768, world, rank)
+    n = b - a
+    xs = [empty(n * H * 4) for _ in range(2)]
+    rs = [empty(n * H * 4) for _ in range(2)]
+    ss = [empty(n * H * 4) for _ in range(2)]
+    os_ = [empty(n * H * 4) for _ in range(2)]
+    w = up(I.gamma(H, 3))
+    for i in range(2):
+        ds3.buffer_write(xs[i], 0, I.normal(4000 + i, (n, H)))
+        ds3.buffer_write(rs[i], 0, I.normal(4100 + i, (n, H)))
+    fns = [lambda i=i: ds3.add_rms_norm(xs[i], rs[i], w, ss[i], os_[i], H, n, eps) for i in range(2)]
+    rec("c4_add_rms_norm_T32768", n, n * 4 * H * 4, time_launches(ds3, fns, 20, max_over_ranks, barrier))
+
+    # C4: Q6_K embed of 32768 ids over the full vocabulary.
+    tab6 = I.q6k_table(V, H, 4200)
+    t6 = ds3.buffer_from_mmap(tab6)
+    bufs.append(t6)
+    del tab6
+    ids = [up(I.token_ids(n, 4300 + i)) for i in range(2)]
+    eo = [os_[i] for i in range(2)]
+    fns = [lambda i=i: ds3.embed_rows(t6, ids[i], eo[i], n, H, V, ds3.TYPE_Q6_K, 1680) for i in range(2)]
+    rec("c4_embed_q6k_T32768", n, n * (1680 + 4 + 4 * H), time_launches(ds3, fns, 20, max_over_ranks, barrier))
+    # Same gather with the Q4_K table and the fused attn_norm.
+    t4 = ds3.buffer_from_mmap(table_q4k)
+    bufs.append(t4)
+    fns = [lambda i=i: ds3.embed_rms_norm(t4, ids[i], w, ss[i], eo[i], n, H, V, ds3.TYPE_Q4_K, 1152, eps)
+           for i in range(2)]
+    rec("embed_q4k_rms_norm_T32768", n, n * (1152 + 4 + 8 * H), time_launches(ds3, fns, 20, max_over_ranks, barrier))
+    for x in xs + rs + ss + os_:
+        x.free()
+    bufs = [x for x in bufs if x not in xs + rs + ss + os_]
+
+    # C5: QK-norm + RoPE on [32768, 32/4, 128] fp32 and fp16 storage, pos 0..32767.
+    qb = empty(n * NQ * HD * 4)
+    kb = empty(n * NK * HD * 4)
+    ds3.buffer_write(qb, 0, I.normal(5000, (n, NQ, HD)))
+    ds3.buffer_write(kb, 0, I.normal(5001, (n, NK, HD)))
+    pos = up(np.arange(a, b, dtype=np.int32))
+    qw, kw = up(I.gamma(HD, 5002)), up(I.gamma(HD, 5003))
+    fn = [lambda: ds3.qk_norm_rope(qb, kb, qw, kw, pos, n, NQ, NK, HD, I.ROPE_THETA, eps)]
+    rec("c5_qk_norm_rope_f32_T32768", n, n * (8 * (NQ + NK) * HD + 4), time_launches(ds3, fn, 20, max_over_ranks, barrier))
+    q16, k16 = empty(n * NQ * HD * 2), empty(n * NK * HD * 2)
+    ds3.buffer_write(q16, 0, I.normal(5004, (n, NQ, HD)).astype(np.float16))
+    ds3.buffer_write(k16, 0, I.normal(5005, (n, NK, HD)).astype(np.float16))
+    fn = [lambda: ds3.qk_norm_rope(q16, k16, qw, kw, pos, n, NQ, NK, HD, I.ROPE_THETA, eps, ds3.TYPE_F16)]
+    rec("c5_qk_norm_rope_f16_T32768", n, n * (4 * (NQ + NK) * HD + 4), time_launches(ds3, fn, 20, max_over_ranks, barrier))
+
+    # C2: decode batch of 64 tokens x 48 layers, one graph (per-layer inputs distinct).
+    L, B2 = 48, 64
+    hid = empty(L * B2 * H * 4)
+    res = empty(L * B2 * H * 4)
+    nrm = empty(L * B2 * H * 4)
+    q2 = empty(L * B2 * NQ * HD * 4)
+    k2 = empty(L * B2 * NK * HD * 4)
+    lg = empty(L * B2 * E * 4)
+    ix = empty(L * B2 * K * 4)
+    sc = empty(L * B2 * K * 4)
+    ds3.buffer_write(hid, 0, I.normal(6000, (L * B2, H)))
+    ds3.buffer_write(res, 0, I.normal(6001, (L * B2, H)))
+    ds3.buffer_write(q2, 0, I.normal(6002, (L * B2, NQ, HD)))
+    ds3.buffer_write(k2, 0, I.normal(6003, (L * B2, NK, HD)))
+    ds3.buffer_write(lg, 0, I.normal(6004, (L * B2, E), 0, 2))
+    pos2 = up(np.tile(I.rng(6005).integers(0, 4096, B2).astype(np.int32), L))
+    views = []
+
+    def view(buf, i, per):
+        v = ds3.buffer_view(buf, i * per, per)
+        views.append(v)
+        return v
+
+    def decode_stack():
+        for l in range(L):
+            ds3.add_rms_norm(view(hid, l, B2 * H * 4), view(res, l, B2 * H * 4), w, view(res, l, B2 * H * 4),
+                             view(nrm, l, B2 * H * 4), H, B2, eps)
+            ds3.qk_norm_rope(view(q2, l, B2 * NQ * HD * 4), view(k2, l, B2 * NK * HD * 4), qw, kw,
+                             view(pos2, l, B2 * 4), B2, NQ, NK, HD, I.ROPE_THETA, eps)
+            ds3.router_softmax_topk(view(lg, l, B2 * E * 4), None, view(ix, l, B2 * K * 4), view(sc, l, B2 * K * 4),
+                                    B2, E, K, True)
+        ds3.rms_norm(view(hid, L - 1, B2 * H * 4), w, view(nrm, L - 1, B2 * H * 4), H, B2, eps)
+
+    c2_bytes = B2 * L * (32768 + 36868 + 576) + B2 * 16384
+    ms = time_launches(ds3, [decode_stack], 1, max_over_ranks, barrier)
+    rec("c2_decode_B64_x48_layers", B2, c2_bytes, ms, note="tokens_per_s counts one 48-layer pass per token")
+    for v in views:
+        v.free()
+
+    for x in bufs:
+        x.free()
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

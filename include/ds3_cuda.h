@@ -44,6 +44,11 @@
 extern "C" {
 #endif
 
+/* The library is built with hidden visibility; only these entry points are exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
 #ifndef DS3_H
 /* GGUF tensor type ids; same values as ds3_type_t in the engine's src/ds3.h:201-216.
  * (When the engine's ds3.h is on the include path its enum is used instead.) */
@@ -263,6 +268,10 @@ const char *ds3_cuda_last_error(void);
 /* Reads and clears the device error word (bit 0: bad token id; bit 1: a
  * bounded wait ran out). Synchronises the module stream. */
 uint32_t ds3_cuda_device_errors(void);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
 
 #ifdef __cplusplus
 }

@@ -52,6 +52,25 @@ __device__ __forceinline__ float rms_inv(float ss, int n, float eps)
     return __fdiv_rn(1.0f, __fsqrt_rn(m));
 }
 
+// Same for a compile-time power-of-two n: ss / n and ss * (1/n) are the same
+// correctly rounded value (scaling by a power of two), so the divide becomes
+// one multiply.
+template <int N>
+__device__ __forceinline__ float rms_inv_pow2(float ss, float eps)
+{
+    static_assert((N & (N - 1)) == 0, "power of two");
+    float m = __fmul_rn(ss, 1.0f / (float)N);
+    m = __fadd_rn(m, eps);
+    return __fdiv_rn(1.0f, __fsqrt_rn(m));
+}
+
+template <int N>
+__device__ __forceinline__ float rms_inv_n(float ss, float eps)
+{
+    if constexpr ((N & (N - 1)) == 0) return rms_inv_pow2<N>(ss, eps);
+    else return rms_inv(ss, N, eps);
+}
+
 // (x * inv) * w, left to right as the reference writes it.
 __device__ __forceinline__ float norm_mul(float x, float inv, float w)
 {
@@ -143,5 +162,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
 }
 
 constexpr uint32_t kWaitLimit = 1u << 22;
+
+// ------------------------------------------------------------------------
+// Programmatic dependent launch (PDL). Every kernel of this library calls
+// pdl_wait() — unconditionally, in every CTA, before any early return and
+// before it touches activations — and then pdl_trigger(). pdl_wait returns
+// once the preceding grid in the stream has completed and its writes are
+// visible, so a chain of PDL launches keeps full stream order for the data;
+// the trigger lets the next kernel be launched and its CTAs made resident
+// while this one works, hiding launch latency. Triggering only after the wait
+// keeps at most one dependent grid waiting behind a running one. Only static
+// parameters (norm weights, embedding table, frequency table) may be read
+// before pdl_wait. Without the PDL launch attribute both are no-ops.
+// ------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 }  // namespace ds3

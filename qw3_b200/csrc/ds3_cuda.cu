@@ -52,6 +52,7 @@ struct State {
     bool batch = false;
     bool capturing = false;
     bool profile = false;
+    bool pdl = true;  // DS3_CUDA_PDL=0 disables programmatic dependent launch
     std::vector<cudaEvent_t> timers;
     std::vector<cudaEvent_t> event_pool;
     std::vector<ProfileRec> prof;
@@ -73,7 +74,7 @@ void set_error(const char *fmt, ...)
 
 bool deferred() { return G.batch || G.capturing; }
 
-ds3::LaunchCtx ctx() { return ds3::LaunchCtx{G.stream, G.err_dev, G.n_sm}; }
+ds3::LaunchCtx ctx() { return ds3::LaunchCtx{G.stream, G.err_dev, G.n_sm, G.pdl}; }
 
 void *dptr(const ds3_cuda_buffer_t *b) { return b ? (void *)(b->base + b->offset) : nullptr; }
 
@@ -243,6 +244,8 @@ int ds3_cuda_init(void)
     G.timers.assign(DS3_CUDA_TIMER_SLOTS, nullptr);
     const char *p = getenv("DS3_CUDA_PROFILE");
     G.profile = p && p[0] == '1';
+    const char *q = getenv("DS3_CUDA_PDL");
+    G.pdl = !(q && q[0] == '0');
     G.inited = true;
     return 0;
 }

@@ -136,7 +136,7 @@ __device__ __forceinline__ void emit_row(float4 *v, int lane, int64_t row, float
 #pragma unroll
         for (int k = 0; k < 2 * NB; k++) ss = f4_sumsq(v[k], ss);
         ss = warp_sum(ss);
-        const float inv = rms_inv(ss, n, eps);
+        const float inv = rms_inv_n<n>(ss, eps);
         const float4 *w4 = reinterpret_cast<const float4 *>(w);
         float4 *o = reinterpret_cast<float4 *>(norm + row * n);
 #pragma unroll
@@ -161,6 +161,8 @@ struct EmbedArgs {
 template <int TYPE, int NB>
 __global__ void __launch_bounds__(kWarps * 32) embed_warp(const EmbedArgs a)
 {
+    pdl_wait();
+    pdl_trigger();
     constexpr int kRowBytes = NB * BlockBytes<TYPE>::v;
     constexpr int kSlot = (kRowBytes + 15) & ~15;
     __shared__ __align__(128) uint8_t slots[kWarps][2][kSlot];
@@ -301,6 +303,8 @@ __global__ void embed_generic(const uint8_t *table, int type, uint64_t row_strid
                               const int32_t *ids, int64_t n_ids, int n_cols, float *out,
                               unsigned *err)
 {
+    pdl_wait();
+    pdl_trigger();
     const int64_t total = n_ids * n_cols;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
          e += (int64_t)gridDim.x * blockDim.x) {
@@ -322,7 +326,7 @@ cudaError_t run_fast(const LaunchCtx &c, const EmbedArgs &a)
     const int64_t need = (a.n_ids + kWarps - 1) / kWarps;
     const int64_t cap = (int64_t)c.n_sm * 8;
     const int64_t blocks = need < cap ? need : cap;
-    embed_warp<TYPE, NB><<<(unsigned)blocks, kWarps * 32, 0, c.stream>>>(a);
+    launch_k(c, embed_warp<TYPE, NB>, dim3((unsigned)blocks), dim3(kWarps * 32), a);
     return cudaGetLastError();
 }
 
@@ -372,7 +376,7 @@ cudaError_t launch_embed(const LaunchCtx &c, const uint8_t *table, int type, uin
     const int64_t total = n_ids * (int64_t)n_cols;
     int64_t blocks = (total + 255) / 256;
     if (blocks > (int64_t)c.n_sm * 32) blocks = (int64_t)c.n_sm * 32;
-    embed_generic<<<(unsigned)blocks, 256, 0, c.stream>>>(table, type, row_stride, n_vocab, ids, n_ids,
+    launch_k(c, embed_generic, dim3((unsigned)blocks), dim3(256), table, type, row_stride, n_vocab, ids, n_ids,
                                                           n_cols, dst, c.err);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || !norm_out) return e;

@@ -12,7 +12,25 @@ struct LaunchCtx {
     cudaStream_t stream;
     unsigned *err;  // device-visible error word (see common.cuh)
     int n_sm;
+    bool pdl;       // launch with programmatic stream serialization
 };
+
+// Launch `k` on c.stream, with the PDL attribute when c.pdl is set.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(const LaunchCtx &c, void (*k)(KArgs...), dim3 grid, dim3 block, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = c.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = c.pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
 
 // x [rows, n] (+ r) -> sum_out (optional), norm_out. r == nullptr: plain RMSNorm.
 cudaError_t launch_add_rms_norm(const LaunchCtx &c, const float *x, const float *r, const float *w,

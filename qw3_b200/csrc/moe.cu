@@ -26,27 +26,32 @@ __device__ __forceinline__ float silu_mul(float g, float u)
 }
 
 // ------------------------------------------------------------------ SwiGLU
-constexpr int kSwigluUnroll = 4;
+// Each thread owns kSwigluUnits float4 units (stride = total threads) and
+// issues all 2 x kSwigluUnits 128-bit loads before computing, so at the
+// 4096 x 768 shape one resident wave holds the whole input in flight.
+constexpr int kSwigluUnits = 4;
 
-__global__ void __launch_bounds__(256) swiglu_vec(const float4 *gate, const float4 *up,
-                                                  const float *row_w, float4 *out, int64_t units,
-                                                  int64_t cols4)
+template <typename Index>
+__global__ void __launch_bounds__(256, 4) swiglu_vec(const float4 *gate, const float4 *up,
+                                                     const float *row_w, float4 *out, Index units,
+                                                     Index cols4)
 {
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    int64_t u0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    for (; u0 < units; u0 += stride * kSwigluUnroll) {
-        float4 g[kSwigluUnroll], v[kSwigluUnroll];
+    pdl_wait();
+    pdl_trigger();
+    const Index stride = (Index)gridDim.x * blockDim.x;
+    for (Index u0 = (Index)blockIdx.x * blockDim.x + threadIdx.x; u0 < units; u0 += stride * kSwigluUnits) {
+        float4 g[kSwigluUnits], v[kSwigluUnits];
 #pragma unroll
-        for (int k = 0; k < kSwigluUnroll; k++) {
-            const int64_t u = u0 + k * stride;
+        for (int k = 0; k < kSwigluUnits; k++) {
+            const Index u = u0 + k * stride;
             if (u < units) {
                 g[k] = ld_stream(gate + u);
                 v[k] = ld_stream(up + u);
             }
         }
 #pragma unroll
-        for (int k = 0; k < kSwigluUnroll; k++) {
-            const int64_t u = u0 + k * stride;
+        for (int k = 0; k < kSwigluUnits; k++) {
+            const Index u = u0 + k * stride;
             if (u >= units) break;
             float4 o = make_float4(silu_mul(g[k].x, v[k].x), silu_mul(g[k].y, v[k].y),
                                    silu_mul(g[k].z, v[k].z), silu_mul(g[k].w, v[k].w));
@@ -62,6 +67,8 @@ __global__ void __launch_bounds__(256) swiglu_vec(const float4 *gate, const floa
 __global__ void swiglu_scalar(const float *gate, const float *up, const float *row_w, float *out,
                               int64_t n, int64_t cols)
 {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         float o = silu_mul(gate[i], up[i]);
@@ -79,6 +86,8 @@ __global__ void __launch_bounds__(128) combine_vec(const float4 *y, const int32_
                                                    float4 *out, int64_t n_tokens, int n_used,
                                                    int64_t cols4)
 {
+    pdl_wait();
+    pdl_trigger();
     const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (e >= n_tokens * cols4) return;
     const int64_t t = e / cols4;
@@ -120,6 +129,8 @@ __global__ void combine_scalar(const float *y, const int32_t *y_rows, const floa
                                const float *residual, float *out, int64_t n_tokens, int n_used,
                                int64_t cols)
 {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_tokens * cols;
          e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t t = e / cols, c = e - t * cols;
@@ -135,6 +146,8 @@ __global__ void combine_scalar(const float *y, const int32_t *y_rows, const floa
 // ----------------------------------------------------------------- vec_add
 __global__ void vec_add_vec(const float4 *a, const float4 *b, float4 *c, int64_t n4)
 {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
          i += (int64_t)gridDim.x * blockDim.x)
         c[i] = f4_add(ld_stream(a + i), ld_stream(b + i));
@@ -142,6 +155,8 @@ __global__ void vec_add_vec(const float4 *a, const float4 *b, float4 *c, int64_t
 
 __global__ void vec_add_scalar(const float *a, const float *b, float *c, int64_t n)
 {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x)
         c[i] = __fadd_rn(a[i], b[i]);
@@ -151,6 +166,8 @@ __global__ void vec_add_scalar(const float *a, const float *b, float *c, int64_t
 __global__ void gather_rows_k(const float *src, const int32_t *ids, float *dst, int64_t n_cols,
                               int64_t count, int64_t n_src_rows, unsigned *err)
 {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < count * n_cols;
          e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i = e / n_cols, j = e - i * n_cols;
@@ -167,6 +184,8 @@ __global__ void gather_rows_k(const float *src, const int32_t *ids, float *dst, 
 __global__ void scatter_add_k(const float *src, const float *scores, const int32_t *ids, float *dst,
                               int64_t n_cols, int64_t count, int64_t n_dst_rows, unsigned *err)
 {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < count * n_cols;
          e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i = e / n_cols, j = e - i * n_cols;
@@ -198,13 +217,27 @@ cudaError_t launch_swiglu(const LaunchCtx &c, const float *gate, const float *up
     if (n <= 0) return cudaSuccess;
     if (cols % 4 == 0 && al16(gate) && al16(up) && al16(out)) {
         const int64_t units = n / 4;
-        // Enough threads for ~4 x 2 x 16 B in flight each across all SMs.
-        const unsigned blocks = grid_for(c, (units + kSwigluUnroll - 1) / kSwigluUnroll, 256, 8);
-        swiglu_vec<<<blocks, 256, 0, c.stream>>>(reinterpret_cast<const float4 *>(gate),
-                                                 reinterpret_cast<const float4 *>(up), row_w,
-                                                 reinterpret_cast<float4 *>(out), units, cols / 4);
+        // One wave: at most as many CTAs as can be resident at once (a second
+        // partial wave would double the latency at small sizes); each thread
+        // then streams units with kSwigluUnroll x 2 loads in flight.
+        const bool small = units < (int64_t)1 << 30;
+        static int occ32 = 0, occ64 = 0;
+        int &occ = small ? occ32 : occ64;
+        if (!occ && cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                        &occ, small ? (const void *)swiglu_vec<uint32_t> : (const void *)swiglu_vec<int64_t>, 256,
+                        0) != cudaSuccess)
+            occ = 4;
+        const unsigned blocks = grid_for(c, (units + kSwigluUnits - 1) / kSwigluUnits, 256, occ > 0 ? occ : 4);
+        auto *g4 = reinterpret_cast<const float4 *>(gate);
+        auto *u4 = reinterpret_cast<const float4 *>(up);
+        auto *o4 = reinterpret_cast<float4 *>(out);
+        if (small)
+            launch_k(c, swiglu_vec<uint32_t>, dim3(blocks), dim3(256), g4, u4, row_w, o4, (uint32_t)units,
+                     (uint32_t)(cols / 4));
+        else
+            launch_k(c, swiglu_vec<int64_t>, dim3(blocks), dim3(256), g4, u4, row_w, o4, units, cols / 4);
     } else {
-        swiglu_scalar<<<grid_for(c, n, 256, 16), 256, 0, c.stream>>>(gate, up, row_w, out, n, cols);
+        launch_k(c, swiglu_scalar, dim3(grid_for(c, n, 256, 16)), dim3(256), gate, up, row_w, out, n, cols);
     }
     return cudaGetLastError();
 }
@@ -222,11 +255,11 @@ cudaError_t launch_combine(const LaunchCtx &c, const float *y, const int32_t *y_
         auto *r4 = reinterpret_cast<const float4 *>(residual);
         auto *o4 = reinterpret_cast<float4 *>(out);
         if (n_used == 8)
-            combine_vec<8><<<blocks, 128, 0, c.stream>>>(y4, y_rows, w, r4, o4, n_tokens, n_used, cols4);
+            launch_k(c, combine_vec<8>, dim3(blocks), dim3(128), y4, y_rows, w, r4, o4, n_tokens, n_used, cols4);
         else
-            combine_vec<0><<<blocks, 128, 0, c.stream>>>(y4, y_rows, w, r4, o4, n_tokens, n_used, cols4);
+            launch_k(c, combine_vec<0>, dim3(blocks), dim3(128), y4, y_rows, w, r4, o4, n_tokens, n_used, cols4);
     } else {
-        combine_scalar<<<grid_for(c, n_tokens * n_cols, 256, 16), 256, 0, c.stream>>>(
+        launch_k(c, combine_scalar, dim3(grid_for(c, n_tokens * n_cols, 256, 16)), dim3(256), 
             y, y_rows, w, residual, out, n_tokens, n_used, n_cols);
     }
     return cudaGetLastError();
@@ -236,11 +269,11 @@ cudaError_t launch_vec_add(const LaunchCtx &c, const float *a, const float *b, f
 {
     if (n <= 0) return cudaSuccess;
     if (n % 4 == 0 && al16(a) && al16(b) && al16(out))
-        vec_add_vec<<<grid_for(c, n / 4, 256, 16), 256, 0, c.stream>>>(
+        launch_k(c, vec_add_vec, dim3(grid_for(c, n / 4, 256, 16)), dim3(256), 
             reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b),
             reinterpret_cast<float4 *>(out), n / 4);
     else
-        vec_add_scalar<<<grid_for(c, n, 256, 16), 256, 0, c.stream>>>(a, b, out, n);
+        launch_k(c, vec_add_scalar, dim3(grid_for(c, n, 256, 16)), dim3(256), a, b, out, n);
     return cudaGetLastError();
 }
 
@@ -248,7 +281,7 @@ cudaError_t launch_gather_rows(const LaunchCtx &c, const float *src, const int32
                                float *dst, int64_t n_cols, int64_t count, int64_t n_src_rows)
 {
     if (count <= 0 || n_cols <= 0) return cudaSuccess;
-    gather_rows_k<<<grid_for(c, count * n_cols, 256, 16), 256, 0, c.stream>>>(src, ids, dst, n_cols, count,
+    launch_k(c, gather_rows_k, dim3(grid_for(c, count * n_cols, 256, 16)), dim3(256), src, ids, dst, n_cols, count,
                                                                              n_src_rows, c.err);
     return cudaGetLastError();
 }
@@ -258,7 +291,7 @@ cudaError_t launch_scatter_add_weighted(const LaunchCtx &c, const float *src, co
                                         int64_t count, int64_t n_dst_rows)
 {
     if (count <= 0 || n_cols <= 0) return cudaSuccess;
-    scatter_add_k<<<grid_for(c, count * n_cols, 256, 16), 256, 0, c.stream>>>(
+    launch_k(c, scatter_add_k, dim3(grid_for(c, count * n_cols, 256, 16)), dim3(256), 
         src, scores, ids, dst, n_cols, count, n_dst_rows, c.err);
     return cudaGetLastError();
 }

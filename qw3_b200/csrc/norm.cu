@@ -20,6 +20,8 @@ __global__ void __launch_bounds__(128) add_rms_norm_warp(const float *x, const f
                                                          const float *w, float *sum_out,
                                                          float *norm_out, int64_t rows, float eps)
 {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -41,7 +43,7 @@ __global__ void __launch_bounds__(128) add_rms_norm_warp(const float *x, const f
 #pragma unroll
     for (int i = 0; i < VPL; i++) ss = f4_sumsq(v[i], ss);
     ss = warp_sum(ss);
-    const float inv = rms_inv(ss, n, eps);
+    const float inv = rms_inv_n<n>(ss, eps);
 
     if (sum_out) {
         float4 *so = reinterpret_cast<float4 *>(sum_out + row * n);
@@ -62,6 +64,8 @@ __global__ void __launch_bounds__(256) add_rms_norm_block(const float *x, const 
                                                           const float *w, float *sum_out,
                                                           float *norm_out, int n, float eps)
 {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float part[32];
     const int64_t row = blockIdx.x;
     const float *xr = x + row * n;
@@ -101,7 +105,7 @@ cudaError_t run_warp(const LaunchCtx &c, const float *x, const float *r, const f
 {
     const int warps = 4;
     const int64_t blocks = (rows + warps - 1) / warps;
-    add_rms_norm_warp<VPL><<<(unsigned)blocks, warps * 32, 0, c.stream>>>(x, r, w, sum_out, norm_out,
+    launch_k(c, add_rms_norm_warp<VPL>, dim3((unsigned)blocks), dim3(warps * 32), x, r, w, sum_out, norm_out,
                                                                           rows, eps);
     return cudaGetLastError();
 }
@@ -129,7 +133,7 @@ cudaError_t launch_add_rms_norm(const LaunchCtx &c, const float *x, const float 
         }
     }
     if (rows > 0x7fffffffLL) return cudaErrorInvalidValue;
-    add_rms_norm_block<<<(unsigned)rows, 256, 0, c.stream>>>(x, r, w, sum_out, norm_out, n, eps);
+    launch_k(c, add_rms_norm_block, dim3((unsigned)rows), dim3(256), x, r, w, sum_out, norm_out, n, eps);
     return cudaGetLastError();
 }
 

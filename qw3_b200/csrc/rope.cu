@@ -5,13 +5,14 @@
 // metal/rope.metal:88-123 with the host frequency table of
 // src/ds3_metal.m:478-489.
 //
-// Fast path (head_dim = 128): one warp owns a group of up to 8 heads of one
-// token; lane l holds elements 4l..4l+3 of each head (one 128-bit load per
-// head, coalesced). RoPE pairs (i, i+64) live in lanes l and l^16, exchanged
-// with one shuffle. The angle of pair i depends only on (position, i), so a
-// warp computes the 64 cos/sin values of its token once (2 sincosf per lane,
-// shared through a shuffle) and reuses them for all its heads. Each element
-// is read once and written once: 2 x 4 B (fp32) or 2 x 2 B (fp16 storage).
+// Fast path (head_dim = 128, qk_norm_rope_tile): a CTA owns 2 tokens. The
+// angle of pair i depends only on (position, i), so the CTA computes the 64
+// cos/sin values of each token once into shared memory. Warps take groups of
+// 4 heads with 8 lanes per head; each lane holds 8 elements of the first half
+// of the head and their 8 RoPE partners (i + 64), loaded with 128-bit
+// accesses that cover 128 contiguous bytes per 8 lanes; the RMS sum needs 3
+// shuffles and the rotation none. Each element is read once and written
+// once: 2 x 4 B (fp32) or 2 x 2 B (fp16).
 //
 // Numerics: freq[i] = powf(theta, (float)i * (-2/hd)) is built on the host
 // with the C library (same as the reference), the angle is the fp32 product
@@ -28,35 +29,6 @@ struct FreqTable {
     float f[256];  // head_dim / 2 entries used (head_dim <= 512)
 };
 
-constexpr int kHeadsPerWarp = 8;
-
-template <typename T>
-struct Vec4;
-template <>
-struct Vec4<float> {
-    __device__ static float4 load(const float *p) { return ld_stream(reinterpret_cast<const float4 *>(p)); }
-    __device__ static void store(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
-};
-template <>
-struct Vec4<__half> {
-    __device__ static float4 load(const __half *p)
-    {
-        const uint2 u = __ldcs(reinterpret_cast<const uint2 *>(p));
-        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
-        const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
-        return make_float4(a.x, a.y, b.x, b.y);
-    }
-    __device__ static void store(__half *p, float4 v)
-    {
-        __half2 a = __floats2half2_rn(v.x, v.y);
-        __half2 b = __floats2half2_rn(v.z, v.w);
-        uint2 u;
-        u.x = *reinterpret_cast<unsigned *>(&a);
-        u.y = *reinterpret_cast<unsigned *>(&b);
-        *reinterpret_cast<uint2 *>(p) = u;
-    }
-};
-
 __device__ __forceinline__ float rot_lo(float own, float other, float c, float s)
 {
     return __fsub_rn(__fmul_rn(own, c), __fmul_rn(other, s));  // x0*c - x1*s
@@ -66,80 +38,176 @@ __device__ __forceinline__ float rot_hi(float own, float other, float c, float s
     return __fadd_rn(__fmul_rn(other, s), __fmul_rn(own, c));  // x0*s + x1*c
 }
 
+// One lane's share of a 128-wide head when 8 lanes hold the head (j = lane
+// within the 8): `lo` = 8 elements from the first half of the head and `hi`
+// = their RoPE partners (index + 64), so the rotation is lane-local. Each
+// load/store instruction of the 8 lanes covers 128 contiguous bytes.
+//   fp32: lo = {4j..4j+3, 32+4j..32+4j+3}, pair index of lo[e] = pidx(j, e)
+//   fp16: lo = {8j..8j+7}
 template <typename T>
-__global__ void __launch_bounds__(128) qk_norm_rope_hd128(
-    const T *q_src, T *q_dst, const T *k_src, T *k_dst, const float *q_w, const float *k_w,
-    const int32_t *pos, int64_t rows, int nq, int nk, int chunks_q, int chunks_k,
-    const __grid_constant__ FreqTable ft, float eps, int do_norm)
-{
-    const int lane = threadIdx.x & 31;
-    const int chunks = chunks_q + chunks_k;
-    const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int64_t t = gw / chunks;
-    if (t >= rows) return;
-    const int ch = (int)(gw - t * chunks);
+struct HeadSlice;
+template <>
+struct HeadSlice<float> {
+    __device__ static int pidx(int j, int e) { return (e < 4) ? 4 * j + e : 32 + 4 * j + (e - 4); }
+    __device__ static void load(const float *head, int j, float *lo, float *hi)
+    {
+        const float4 *q = reinterpret_cast<const float4 *>(head);
+        const float4 a = ld_stream(q + j), b = ld_stream(q + 8 + j);
+        const float4 c = ld_stream(q + 16 + j), d = ld_stream(q + 24 + j);
+        lo[0] = a.x; lo[1] = a.y; lo[2] = a.z; lo[3] = a.w;
+        lo[4] = b.x; lo[5] = b.y; lo[6] = b.z; lo[7] = b.w;
+        hi[0] = c.x; hi[1] = c.y; hi[2] = c.z; hi[3] = c.w;
+        hi[4] = d.x; hi[5] = d.y; hi[6] = d.z; hi[7] = d.w;
+    }
+    __device__ static void store(float *head, int j, const float *lo, const float *hi)
+    {
+        float4 *q = reinterpret_cast<float4 *>(head);
+        q[j] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+        q[8 + j] = make_float4(lo[4], lo[5], lo[6], lo[7]);
+        q[16 + j] = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        q[24 + j] = make_float4(hi[4], hi[5], hi[6], hi[7]);
+    }
+};
+template <>
+struct HeadSlice<__half> {
+    __device__ static int pidx(int j, int e) { return 8 * j + e; }
+    __device__ static void unpack(uint4 u, float *v)
+    {
+        const unsigned w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[k]));
+            v[2 * k] = f.x;
+            v[2 * k + 1] = f.y;
+        }
+    }
+    __device__ static uint4 pack(const float *v)
+    {
+        unsigned w[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+            w[k] = *reinterpret_cast<unsigned *>(&h);
+        }
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    __device__ static void load(const __half *head, int j, float *lo, float *hi)
+    {
+        const uint4 *q = reinterpret_cast<const uint4 *>(head);
+        unpack(__ldcs(q + j), lo);
+        unpack(__ldcs(q + 8 + j), hi);
+    }
+    __device__ static void store(__half *head, int j, const float *lo, const float *hi)
+    {
+        uint4 *q = reinterpret_cast<uint4 *>(head);
+        q[j] = pack(lo);
+        q[8 + j] = pack(hi);
+    }
+};
 
-    const T *src;
-    T *dst;
-    const float *w;
-    int h0, nh;
-    if (ch < chunks_q) {
-        h0 = ch * kHeadsPerWarp;
-        nh = min(kHeadsPerWarp, nq - h0);
-        src = q_src + (t * nq + h0) * 128;
-        dst = q_dst + (t * nq + h0) * 128;
-        w = q_w;
-    } else {
-        h0 = (ch - chunks_q) * kHeadsPerWarp;
-        nh = min(kHeadsPerWarp, nk - h0);
-        src = k_src + (t * nk + h0) * 128;
-        dst = k_dst + (t * nk + h0) * 128;
-        w = k_w;
+// head_dim = 128. A CTA of kTileWarps warps owns kTileTok tokens. While the
+// head rows are being loaded, the CTA computes the cos/sin of the 64 rotation
+// pairs of each of its tokens once into shared memory (one sincosf per pair).
+// Each warp handles groups of 4 heads, 8 lanes per head (HeadSlice layout):
+// the RMS sum is 3 shuffles and the rotation needs no data exchange.
+constexpr int kTileTok = 2;
+constexpr int kTileWarps = 9;
+constexpr int kMaxGroupsPerWarp = 2;  // 2 tokens x 36 heads = 18 groups = 9 warps x 2
+
+template <typename T>
+__global__ void __launch_bounds__(kTileWarps * 32, sizeof(T) == 2 ? 4 : 3) qk_norm_rope_tile(
+    const T *q_src, T *q_dst, const T *k_src, T *k_dst, const float *q_w, const float *k_w,
+    const int32_t *pos, int64_t rows, int nq, int nk, const __grid_constant__ FreqTable ft, float eps,
+    int do_norm)
+{
+    __shared__ __align__(16) float cs[kTileTok][64];
+    __shared__ __align__(16) float sn[kTileTok][64];
+    __shared__ __align__(16) float wq[128];
+    __shared__ __align__(16) float wk[128];
+
+    const int tid = threadIdx.x;
+    if (do_norm) {  // static parameters: safe to read before the wait
+        if (tid < 128) wq[tid] = q_w[tid];
+        else if (tid < 256 && nk > 0) wk[tid - 128] = k_w[tid - 128];
+    }
+    pdl_wait();
+    pdl_trigger();
+
+    const int64_t t0 = (int64_t)blockIdx.x * kTileTok;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int sub = lane >> 3;  // head within the group of 4
+    const int j = lane & 7;     // slice of the head
+    const int nh = nq + nk;
+    const int n_heads = kTileTok * nh;
+    const int n_groups = (n_heads + 3) >> 2;
+
+    float lo[kMaxGroupsPerWarp][8], hi[kMaxGroupsPerWarp][8];
+    T *headp[kMaxGroupsPerWarp];
+    int meta[kMaxGroupsPerWarp];  // bit 0: active, bit 1: K head, bits 2+: local token
+#pragma unroll
+    for (int gi = 0; gi < kMaxGroupsPerWarp; gi++) {
+        const int g = warp + gi * kTileWarps;
+        const int h = 4 * g + sub;
+        meta[gi] = 0;
+        headp[gi] = nullptr;
+        if (g < n_groups && h < n_heads) {
+            const int tl = h / nh, hh = h - tl * nh;
+            const int64_t t = t0 + tl;
+            if (t < rows) {
+                const bool is_k = hh >= nq;
+                const int64_t off = is_k ? (t * nk + (hh - nq)) * 128 : (t * nq + hh) * 128;
+                headp[gi] = (is_k ? k_dst : q_dst) + off;
+                meta[gi] = 1 | (is_k ? 2 : 0) | (tl << 2);
+                HeadSlice<T>::load((is_k ? k_src : q_src) + off, j, lo[gi], hi[gi]);
+            }
+        }
+        if (!(meta[gi] & 1)) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) lo[gi][e] = hi[gi][e] = 0.0f;
+        }
     }
 
-    float4 v[kHeadsPerWarp];
-#pragma unroll
-    for (int h = 0; h < kHeadsPerWarp; h++)
-        if (h < nh) v[h] = Vec4<T>::load(src + h * 128 + 4 * lane);
-
-    // cos/sin of pairs i = 4*(lane&15) + j: lanes < 16 compute j = 0,1, lanes
-    // >= 16 compute j = 2,3, then swap halves with lane^16.
-    const float p = (float)pos[t];
-    const int ib = 4 * (lane & 15) + ((lane < 16) ? 0 : 2);
-    float s0, c0, s1, c1;
-    sincosf(__fmul_rn(p, ft.f[ib]), &s0, &c0);
-    sincosf(__fmul_rn(p, ft.f[ib + 1]), &s1, &c1);
-    const float os0 = __shfl_xor_sync(kFull, s0, 16), oc0 = __shfl_xor_sync(kFull, c0, 16);
-    const float os1 = __shfl_xor_sync(kFull, s1, 16), oc1 = __shfl_xor_sync(kFull, c1, 16);
-    const bool lo = lane < 16;
-    const float cs[4] = {lo ? c0 : oc0, lo ? c1 : oc1, lo ? oc0 : c0, lo ? oc1 : c1};
-    const float sn[4] = {lo ? s0 : os0, lo ? s1 : os1, lo ? os0 : s0, lo ? os1 : s1};
-
-    float4 wv = make_float4(1.f, 1.f, 1.f, 1.f);
-    if (do_norm) wv = ld_param(reinterpret_cast<const float4 *>(w) + lane);
+    // cos/sin of this tile's tokens, computed while the loads above are in flight
+    if (tid < kTileTok * 64) {
+        const int tl = tid >> 6, i = tid & 63;
+        const int64_t t = t0 + tl;
+        float s = 0.0f, c = 1.0f;
+        if (t < rows) sincosf(__fmul_rn((float)pos[t], ft.f[i]), &s, &c);
+        cs[tl][i] = c;
+        sn[tl][i] = s;
+    }
+    __syncthreads();
 
 #pragma unroll
-    for (int h = 0; h < kHeadsPerWarp; h++) {
-        if (h >= nh) break;
-        float4 x = v[h];
+    for (int gi = 0; gi < kMaxGroupsPerWarp; gi++) {
+        if (warp + gi * kTileWarps >= n_groups) break;  // warp-uniform
+        float *xl = lo[gi], *xh = hi[gi];
         if (do_norm) {
-            const float ss = warp_sum(f4_sumsq(x, 0.0f));
-            x = f4_norm(x, rms_inv(ss, 128, eps), wv);
+            float ss = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; e++) ss = sq_acc(sq_acc(ss, xl[e]), xh[e]);
+            ss += __shfl_xor_sync(kFull, ss, 1);
+            ss += __shfl_xor_sync(kFull, ss, 2);
+            ss += __shfl_xor_sync(kFull, ss, 4);
+            const float inv = rms_inv_pow2<128>(ss, eps);
+            const float *w = (meta[gi] & 2) ? wk : wq;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const int pi = HeadSlice<T>::pidx(j, e);
+                xl[e] = norm_mul(xl[e], inv, w[pi]);
+                xh[e] = norm_mul(xh[e], inv, w[pi + 64]);
+            }
         }
-        float4 o;
-        o.x = __shfl_xor_sync(kFull, x.x, 16);
-        o.y = __shfl_xor_sync(kFull, x.y, 16);
-        o.z = __shfl_xor_sync(kFull, x.z, 16);
-        o.w = __shfl_xor_sync(kFull, x.w, 16);
-        float4 y;
-        if (lo) {
-            y = make_float4(rot_lo(x.x, o.x, cs[0], sn[0]), rot_lo(x.y, o.y, cs[1], sn[1]),
-                            rot_lo(x.z, o.z, cs[2], sn[2]), rot_lo(x.w, o.w, cs[3], sn[3]));
-        } else {
-            y = make_float4(rot_hi(x.x, o.x, cs[0], sn[0]), rot_hi(x.y, o.y, cs[1], sn[1]),
-                            rot_hi(x.z, o.z, cs[2], sn[2]), rot_hi(x.w, o.w, cs[3], sn[3]));
+        const int tl = meta[gi] >> 2;
+        float yl[8], yh[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int pi = HeadSlice<T>::pidx(j, e);
+            const float c = cs[tl][pi], s = sn[tl][pi];
+            yl[e] = rot_lo(xl[e], xh[e], c, s);  // x0*c - x1*s
+            yh[e] = rot_hi(xh[e], xl[e], c, s);  // x0*s + x1*c
         }
-        Vec4<T>::store(dst + h * 128 + 4 * lane, y);
+        if (meta[gi] & 1) HeadSlice<T>::store(headp[gi], j, yl, yh);
     }
 }
 
@@ -164,6 +232,8 @@ __global__ void qk_norm_rope_generic(const T *q_src, T *q_dst, const T *k_src, T
                                      int nq, int nk, int hd, const __grid_constant__ FreqTable ft,
                                      float eps, int do_norm)
 {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float part[32];
     const int64_t t = blockIdx.x;
     const int head = blockIdx.y;
@@ -214,17 +284,13 @@ cudaError_t run(const LaunchCtx &c, const void *qs, void *qd, const void *ks, vo
                 int nk, int hd, int use_hd128, const FreqTable &ft, float eps, int do_norm)
 {
     if (use_hd128) {
-        const int cq = (nq + kHeadsPerWarp - 1) / kHeadsPerWarp;
-        const int ck = (nk + kHeadsPerWarp - 1) / kHeadsPerWarp;
-        const int64_t warps = rows * (cq + ck);
-        const int64_t blocks = (warps + 3) / 4;
-        qk_norm_rope_hd128<T><<<(unsigned)blocks, 128, 0, c.stream>>>(
-            (const T *)qs, (T *)qd, (const T *)ks, (T *)kd, q_w, k_w, pos, rows, nq, nk, cq, ck, ft,
-            eps, do_norm);
+        const int64_t blocks = (rows + kTileTok - 1) / kTileTok;
+        launch_k(c, qk_norm_rope_tile<T>, dim3((unsigned)blocks), dim3(kTileWarps * 32), (const T *)qs, (T *)qd,
+                 (const T *)ks, (T *)kd, q_w, k_w, pos, rows, nq, nk, ft, eps, do_norm);
     } else {
         dim3 grid((unsigned)rows, (unsigned)(nq + nk));
         const int threads = ((hd / 2 + 31) / 32) * 32;
-        qk_norm_rope_generic<T><<<grid, threads, 0, c.stream>>>((const T *)qs, (T *)qd, (const T *)ks,
+        launch_k(c, qk_norm_rope_generic<T>, dim3(grid), dim3(threads), (const T *)qs, (T *)qd, (const T *)ks,
                                                                 (T *)kd, q_w, k_w, pos, nq, nk, hd, ft,
                                                                 eps, do_norm);
     }
@@ -243,13 +309,15 @@ cudaError_t launch_qk_norm_rope(const LaunchCtx &c, const void *q_src, void *q_d
     if (hd <= 0 || hd % 2 || hd > 512 || rows > 0x7fffffffLL) return cudaErrorInvalidValue;
     FreqTable ft;
     for (int i = 0; i < hd / 2; i++) ft.f[i] = freq[i];
-    // The 128-wide kernel moves 4 elements per lane: 16 B (fp32) or 8 B (fp16)
-    // per access, and reads the norm weights as float4.
-    const uintptr_t m = storage ? 7u : 15u;
+    // The 128-wide kernel moves 16 contiguous elements per lane with 16-byte
+    // accesses, so head rows must be 16-byte aligned.
+    const uintptr_t m = 15u;
     const uintptr_t data = reinterpret_cast<uintptr_t>(q_src) | reinterpret_cast<uintptr_t>(q_dst) |
                            reinterpret_cast<uintptr_t>(k_src) | reinterpret_cast<uintptr_t>(k_dst);
     const uintptr_t wts = reinterpret_cast<uintptr_t>(q_w) | reinterpret_cast<uintptr_t>(k_w);
-    const int use_hd = (hd == 128 && (data & m) == 0 && (!do_norm || (wts & 15u) == 0)) ? 128 : 0;
+    const int groups = (kTileTok * (nq + nk) + 3) / 4;
+    const int use_hd = (hd == 128 && (data & m) == 0 && groups <= kTileWarps * kMaxGroupsPerWarp) ? 128 : 0;
+    (void)wts;
     if (storage)
         return run<__half>(c, q_src, q_dst, k_src, k_dst, q_w, k_w, pos, rows, nq, nk, hd, use_hd, ft, eps,
                            do_norm);

@@ -23,6 +23,13 @@
 namespace ds3 {
 namespace {
 
+// Monotone map of a (non-NaN) float onto unsigned integers.
+__device__ __forceinline__ unsigned order_key(float x)
+{
+    const unsigned u = __float_as_uint(x);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi)
 {
     if (i == INT_MAX) return false;
@@ -35,6 +42,8 @@ __global__ void __launch_bounds__(128) router_warp(const float *logits, float *p
                                                    int32_t *idx, float *scores, int64_t n_tokens,
                                                    int n_used, int norm_topk)
 {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= n_tokens) return;
@@ -81,30 +90,30 @@ __global__ void __launch_bounds__(128) router_warp(const float *logits, float *p
         }
     }
 
+    // Selection keys: the float order of the logits as unsigned integers, so a
+    // round is a local scan plus one redux.sync max and one ballot (lowest
+    // lane = lowest expert index among equal logits; -0 is folded into +0).
+    unsigned key[V];
+#pragma unroll
+    for (int j = 0; j < V; j++) key[j] = order_key(__fadd_rn(x[j], 0.0f));
     unsigned used = 0;
     int my_idx = -1;
     float my_sc = 0.0f;
     float sum_sel = 0.0f;
     for (int k = 0; k < n_used; k++) {
-        float bv = 0.0f;
-        int bi = INT_MAX;
+        unsigned best = 0;
+        int bj = -1;
 #pragma unroll
         for (int j = 0; j < V; j++)
-            if (!((used >> j) & 1u) && better(x[j], lane * V + j, bv, bi)) {
-                bv = x[j];
-                bi = lane * V + j;
+            if (!((used >> j) & 1u) && key[j] > best) {
+                best = key[j];
+                bj = j;
             }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(kFull, bv, o);
-            const int oi = __shfl_xor_sync(kFull, bi, o);
-            if (better(ov, oi, bv, bi)) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        if (bi == INT_MAX) break;  // fewer experts than n_used (host rejects this)
-        const int owner = bi / V, sel = bi - owner * V;
+        const unsigned m = __reduce_max_sync(kFull, best);
+        const unsigned ball = __ballot_sync(kFull, bj >= 0 && best == m);
+        if (ball == 0) break;  // fewer experts than n_used (host rejects this)
+        const int owner = __ffs(ball) - 1;
+        const int sel = __shfl_sync(kFull, bj, owner);
         float pj = p[0];
 #pragma unroll
         for (int j = 1; j < V; j++)
@@ -113,7 +122,7 @@ __global__ void __launch_bounds__(128) router_warp(const float *logits, float *p
         const float sc = __shfl_sync(kFull, pj, owner);
         sum_sel = __fadd_rn(sum_sel, sc);
         if (lane == k) {
-            my_idx = bi;
+            my_idx = owner * V + sel;
             my_sc = sc;
         }
     }
@@ -129,6 +138,8 @@ __global__ void __launch_bounds__(128) router_warp(const float *logits, float *p
 __global__ void router_thread(const float *logits, float *probs_out, int32_t *idx, float *scores,
                               int64_t n_tokens, int E, int n_used, int norm_topk)
 {
+    pdl_wait();
+    pdl_trigger();
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= n_tokens) return;
     const float *row = logits + t * E;
@@ -168,7 +179,7 @@ cudaError_t run_warp(const LaunchCtx &c, const float *logits, float *probs, int3
                      float *scores, int64_t n, int n_used, int norm)
 {
     const int64_t blocks = (n + 3) / 4;
-    router_warp<V><<<(unsigned)blocks, 128, 0, c.stream>>>(logits, probs, idx, scores, n, n_used, norm);
+    launch_k(c, router_warp<V>, dim3((unsigned)blocks), dim3(128), logits, probs, idx, scores, n, n_used, norm);
     return cudaGetLastError();
 }
 
@@ -190,7 +201,7 @@ cudaError_t launch_router_topk(const LaunchCtx &c, const float *logits, float *p
         }
     }
     const int64_t blocks = (n_tokens + 127) / 128;
-    router_thread<<<(unsigned)blocks, 128, 0, c.stream>>>(logits, probs_out, idx, scores, n_tokens,
+    launch_k(c, router_thread, dim3((unsigned)blocks), dim3(128), logits, probs_out, idx, scores, n_tokens,
                                                           n_expert, n_used, norm_topk);
     return cudaGetLastError();
 }
