@@ -30,6 +30,24 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found (set NVCC or install the CUDA toolkit)")
 
 
+HOST_SRC = PKG / "host" / "ds3_chunk_pre.c"
+HOST_BIN = PKG / "host" / "ds3_chunk_pre"
+
+
+def build_host() -> Path:
+    """The C host driver, linked against libds3cuda.so (found via rpath)."""
+    if HOST_BIN.exists() and HOST_BIN.stat().st_mtime > max(HOST_SRC.stat().st_mtime, LIB.stat().st_mtime):
+        return HOST_BIN
+    cc = shutil.which("gcc") or "cc"
+    cmd = [cc, "-O2", "-std=c11", "-Wall", "-Wextra", "-I", str(ROOT / "include"), str(HOST_SRC),
+           "-L", str(PKG), "-lds3cuda", "-Wl,-rpath,$ORIGIN/..", "-o", str(HOST_BIN)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError("building the C host driver failed")
+    return HOST_BIN
+
+
 def needs_rebuild() -> bool:
     if not LIB.exists():
         return True
@@ -65,4 +83,5 @@ def build(force: bool = False, ptxas_verbose: bool = False) -> Path:
 
 if __name__ == "__main__":
     build(force=True, ptxas_verbose="--verbose-ptxas" in sys.argv)
+    build_host()
     print(LIB)
