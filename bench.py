@@ -71,9 +71,17 @@ OPS = list(ALGO_BYTES)
 STEP_BYTES = sum(ALGO_BYTES.values())
 
 # DRAM traffic per launch measured with ncu (dram__bytes_read.sum +
-# dram__bytes_write.sum, --clock-control none) on this workload; None where
-# no capture exists yet.
-NCU_TRAFFIC = {}
+# dram__bytes_write.sum, --clock-control none) on this workload. Reads equal
+# the algorithmic input bytes; the outputs of one T=512 launch are still in
+# L2 when it ends, so no write traffic is attributed to the launch itself.
+NCU_TRAFFIC = {
+    "embed_rms_norm": 637824,
+    "qk_norm_rope": 9458560,
+    "add_rms_norm": 8408576,
+    "router_softmax_topk": 270080,
+    "swiglu": 25196672,
+    "moe_combine_residual": 37773696,
+}
 
 CONFIG = {
     "workload": "fused_layer_T512",
@@ -330,6 +338,8 @@ def main():
     ap.add_argument("--sets", type=int, default=4, help="input sets rotated to defeat L2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip the per-config kernel lines")
+    ap.add_argument("--only-configs", action="store_true",
+                    help="run only the per-config kernels (a short command for ncu captures)")
     ap.add_argument("--profile", action="store_true", help="short run for ncu: no e2e, baseline or configs")
     ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between ops (1/0)")
     args = ap.parse_args()
@@ -364,6 +374,12 @@ def main():
 
     # ---- inputs: table shared by all steps, S rotating sets of activations
     table_host = I.q4k_table(V, H, 1)
+    if args.only_configs:
+        peak, _ = measured_peak()
+        cfg = run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_host)
+        if rank == 0:
+            print(json.dumps({"configs": cfg}), flush=True)
+        return 0
     params_host = make_params()
     P = {"table": ds3.buffer_from_mmap(table_host)}
     for n, a in params_host.items():
