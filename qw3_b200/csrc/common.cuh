@@ -105,6 +105,20 @@ __device__ __forceinline__ float4 f4_norm(float4 v, float inv, float4 w)
 __device__ __forceinline__ float4 ld_stream(const float4 *p) { return __ldcs(p); }
 __device__ __forceinline__ float4 ld_param(const float4 *p) { return __ldg(p); }
 
+// Same load as ld_stream, as a volatile asm statement: the compiler keeps
+// such loads in program order, so a kernel that issues a batch of them before
+// using any result really has the whole batch in flight (the scheduler may
+// otherwise interleave loads with their uses to save registers, turning one
+// DRAM round trip into several).
+__device__ __forceinline__ float4 ld_stream_inflight(const float4 *p)
+{
+    float4 v;
+    asm volatile("ld.global.cs.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
 // ------------------------------------------------------------------------
 // mbarrier + bulk async copy (TMA, 1-D) helpers.
 // ------------------------------------------------------------------------

@@ -170,8 +170,9 @@ __global__ void __launch_bounds__(kWarps * 32) embed_warp(const EmbedArgs a)
 
     const int lane = threadIdx.x & 31;
     const int wid = threadIdx.x >> 5;
-    const int64_t stride = (int64_t)gridDim.x * kWarps;
-    int64_t cur = (int64_t)blockIdx.x * kWarps + wid;
+    const int warps = blockDim.x >> 5;  // <= kWarps
+    const int64_t stride = (int64_t)gridDim.x * warps;
+    int64_t cur = (int64_t)blockIdx.x * warps + wid;
     if (cur >= a.n_ids) return;  // whole warp leaves together; no CTA barrier below
 
     float4 v[2 * NB];
@@ -323,10 +324,12 @@ __global__ void embed_generic(const uint8_t *table, int type, uint64_t row_strid
 template <int TYPE, int NB>
 cudaError_t run_fast(const LaunchCtx &c, const EmbedArgs &a)
 {
-    const int64_t need = (a.n_ids + kWarps - 1) / kWarps;
+    // Few rows: one warp per CTA so the rows spread over every SM.
+    const int warps = a.n_ids < 8 * (int64_t)c.n_sm ? 1 : kWarps;
+    const int64_t need = (a.n_ids + warps - 1) / warps;
     const int64_t cap = (int64_t)c.n_sm * 8;
     const int64_t blocks = need < cap ? need : cap;
-    launch_k(c, embed_warp<TYPE, NB>, dim3((unsigned)blocks), dim3(kWarps * 32), a);
+    launch_k(c, embed_warp<TYPE, NB>, dim3((unsigned)blocks), dim3(warps * 32), a);
     return cudaGetLastError();
 }
 

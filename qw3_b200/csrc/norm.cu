@@ -8,6 +8,7 @@
 // once and sum/normed are written exactly once: 16 B/elem for add+norm with
 // the sum stored, 8 B/elem for a plain norm. Loads are 128-bit, coalesced
 // (lane l reads float4 l, l+32, ...), all issued before the first use.
+// Rows of 1024+ elements use add_rms_norm_bulk (TMA-staged rows, below).
 // Generic path (any n): one CTA per row, two passes (the second hits L1/L2).
 #include "common.cuh"
 #include "launch.h"
@@ -30,12 +31,12 @@ __global__ void __launch_bounds__(128) add_rms_norm_warp(const float *x, const f
 
     float4 v[VPL];
 #pragma unroll
-    for (int i = 0; i < VPL; i++) v[i] = ld_stream(xr + i * 32 + lane);
+    for (int i = 0; i < VPL; i++) v[i] = ld_stream_inflight(xr + i * 32 + lane);
     if (r) {
         const float4 *rr = reinterpret_cast<const float4 *>(r + row * n);
         float4 b[VPL];
 #pragma unroll
-        for (int i = 0; i < VPL; i++) b[i] = ld_stream(rr + i * 32 + lane);
+        for (int i = 0; i < VPL; i++) b[i] = ld_stream_inflight(rr + i * 32 + lane);
 #pragma unroll
         for (int i = 0; i < VPL; i++) v[i] = f4_add(v[i], b[i]);
     }
@@ -54,6 +55,94 @@ __global__ void __launch_bounds__(128) add_rms_norm_warp(const float *x, const f
     float4 *no = reinterpret_cast<float4 *>(norm_out + row * n);
 #pragma unroll
     for (int i = 0; i < VPL; i++) no[i * 32 + lane] = f4_norm(v[i], inv, ld_param(w4 + i * 32 + lane));
+}
+
+// Rows of 1024+ elements: x (and r) rows are staged in shared memory by bulk
+// async copies (TMA, 1-D, no multicast) completing on a per-CTA mbarrier, two
+// slots per CTA, so the next row is in flight while the current one is
+// reduced and written. The bytes in flight no longer depend on registers
+// (a row-in-registers warp cannot hold both x and r: the compiler then loads
+// r only after x has arrived, two DRAM round trips). One warp per CTA;
+// a persistent grid of up to kBulkCtasPerSm CTAs per SM strides over rows.
+constexpr int kBulkCtasPerSm = 7;
+
+template <int VPL>
+__global__ void __launch_bounds__(32) add_rms_norm_bulk(const float *x, const float *r, const float *w,
+                                                        float *sum_out, float *norm_out, int64_t rows,
+                                                        float eps, unsigned *err)
+{
+    constexpr int n = VPL * 128;
+    constexpr uint32_t kRowBytes = n * sizeof(float);
+    __shared__ __align__(128) float4 buf[2][2][n / 4];  // [slot][x|r][row]
+    __shared__ __align__(8) uint64_t bars[2];
+    const int lane = threadIdx.x;
+    if (lane == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        mbar_init_fence();
+    }
+    __syncwarp();
+    pdl_wait();
+    pdl_trigger();
+
+    const int64_t stride = gridDim.x;
+    int64_t cur = blockIdx.x;
+    if (cur >= rows) return;
+    const uint32_t bytes = r ? 2 * kRowBytes : kRowBytes;
+    auto issue = [&](int s, int64_t row) {
+        if (lane == 0) {
+            mbar_expect_tx(&bars[s], bytes);
+            bulk_g2s(buf[s][0], x + row * n, kRowBytes, &bars[s]);
+            if (r) bulk_g2s(buf[s][1], r + row * n, kRowBytes, &bars[s]);
+        }
+    };
+    uint32_t parity = 0;
+    int slot = 0;
+    issue(0, cur);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    for (; cur < rows; cur += stride, slot ^= 1) {
+        const int64_t nxt = cur + stride;
+        if (nxt < rows) issue(slot ^ 1, nxt);
+        const bool done = __all_sync(kFull, mbar_wait(&bars[slot], (parity >> slot) & 1u, kWaitLimit));
+        parity ^= 1u << slot;
+        if (!done) {
+            if (lane == 0) flag_error(err, kErrWaitTimeout);
+            mbar_wait(&bars[slot], ((parity >> slot) & 1u) ^ 1u, kWaitLimit);
+            if (nxt < rows) mbar_wait(&bars[slot ^ 1], (parity >> (slot ^ 1)) & 1u, kWaitLimit);
+            return;
+        }
+        float4 v[VPL];
+#pragma unroll
+        for (int i = 0; i < VPL; i++) {
+            v[i] = buf[slot][0][i * 32 + lane];
+            if (r) v[i] = f4_add(v[i], buf[slot][1][i * 32 + lane]);
+        }
+        __syncwarp();  // slot free for the copy issued next iteration
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPL; i++) ss = f4_sumsq(v[i], ss);
+        ss = warp_sum(ss);
+        const float inv = rms_inv_n<n>(ss, eps);
+        if (sum_out) {
+            float4 *so = reinterpret_cast<float4 *>(sum_out + cur * n);
+#pragma unroll
+            for (int i = 0; i < VPL; i++) so[i * 32 + lane] = v[i];
+        }
+        float4 *no = reinterpret_cast<float4 *>(norm_out + cur * n);
+#pragma unroll
+        for (int i = 0; i < VPL; i++) no[i * 32 + lane] = f4_norm(v[i], inv, ld_param(w4 + i * 32 + lane));
+    }
+}
+
+template <int VPL>
+cudaError_t run_bulk(const LaunchCtx &c, const float *x, const float *r, const float *w, float *sum_out,
+                     float *norm_out, int64_t rows, float eps)
+{
+    const int64_t cap = (int64_t)c.n_sm * kBulkCtasPerSm;
+    const int64_t blocks = rows < cap ? rows : cap;
+    launch_k(c, add_rms_norm_bulk<VPL>, dim3((unsigned)blocks), dim3(32), x, r, w, sum_out, norm_out, rows, eps,
+             c.err);
+    return cudaGetLastError();
 }
 
 // Any n. Pass 1: s = x (+ r), written to sum_out when given, sum of squares.
@@ -103,7 +192,9 @@ template <int VPL>
 cudaError_t run_warp(const LaunchCtx &c, const float *x, const float *r, const float *w,
                      float *sum_out, float *norm_out, int64_t rows, float eps)
 {
-    const int warps = 4;
+    // Few rows (a 512-token chunk): one warp per CTA so the rows spread over
+    // every SM; many rows: 4 warps per CTA.
+    const int warps = rows < 8 * (int64_t)c.n_sm ? 1 : 4;
     const int64_t blocks = (rows + warps - 1) / warps;
     launch_k(c, add_rms_norm_warp<VPL>, dim3((unsigned)blocks), dim3(warps * 32), x, r, w, sum_out, norm_out,
                                                                           rows, eps);
@@ -120,15 +211,23 @@ cudaError_t launch_add_rms_norm(const LaunchCtx &c, const float *x, const float 
     if (rows <= 0 || n <= 0) return cudaSuccess;
     const bool vec = (n % 128) == 0 && aligned16(x) && aligned16(w) && aligned16(norm_out) &&
                      (!r || aligned16(r)) && (!sum_out || aligned16(sum_out));
+    // Up to a few thousand rows the TMA-staged kernel wins (it keeps every row
+    // in flight at once); beyond that the row-in-registers kernel reaches the
+    // copy peak through occupancy alone (measured: T=512 5.3 vs 7.0 us,
+    // T=32768 183 vs 167 us).
+    const bool bulk = rows <= 16 * (int64_t)c.n_sm;
     if (vec) {
         switch (n / 128) {
         case 1: return run_warp<1>(c, x, r, w, sum_out, norm_out, rows, eps);
         case 2: return run_warp<2>(c, x, r, w, sum_out, norm_out, rows, eps);
         case 4: return run_warp<4>(c, x, r, w, sum_out, norm_out, rows, eps);
         case 6: return run_warp<6>(c, x, r, w, sum_out, norm_out, rows, eps);
-        case 8: return run_warp<8>(c, x, r, w, sum_out, norm_out, rows, eps);
-        case 12: return run_warp<12>(c, x, r, w, sum_out, norm_out, rows, eps);
-        case 16: return run_warp<16>(c, x, r, w, sum_out, norm_out, rows, eps);
+        case 8: return bulk ? run_bulk<8>(c, x, r, w, sum_out, norm_out, rows, eps)
+                       : run_warp<8>(c, x, r, w, sum_out, norm_out, rows, eps);
+        case 12: return bulk ? run_bulk<12>(c, x, r, w, sum_out, norm_out, rows, eps)
+                       : run_warp<12>(c, x, r, w, sum_out, norm_out, rows, eps);
+        case 16: return bulk ? run_bulk<16>(c, x, r, w, sum_out, norm_out, rows, eps)
+                       : run_warp<16>(c, x, r, w, sum_out, norm_out, rows, eps);
         default: break;
         }
     }

@@ -160,7 +160,7 @@ def test_rms_norm(ds3, B, port, rows, n):
     assert_close(f32(xb, ds3, x.shape), port.rms_norm_rows(x, w, 1e-6))
 
 
-@pytest.mark.parametrize("rows,n", [(64, 2048), (1, 2048), (17, 2048), (6, 1000)])
+@pytest.mark.parametrize("rows,n", [(64, 2048), (1, 2048), (17, 2048), (6, 1000), (3000, 2048), (2500, 1024)])
 def test_add_rms_norm(ds3, B, port, rows, n):
     x, r, w = I.normal(1, (rows, n)), I.normal(2, (rows, n)), I.gamma(n, 3)
     s_want, n_want = port.add_rms_norm(x, r, w, 1e-6)
@@ -304,7 +304,8 @@ def test_router_ties_take_lowest_index(ds3, B, port):
 
 
 # ------------------------------------------------------------ SwiGLU / combine
-@pytest.mark.parametrize("R,Cc,weighted", [(4096, 768, True), (512, 6144, False), (3, 5, True), (1, 1023, False)])
+@pytest.mark.parametrize("R,Cc,weighted", [(4096, 768, True), (512, 6144, False), (3, 5, True), (1, 1023, False),
+                                         (7, 12, True), (40000, 768, True)])
 def test_swiglu(ds3, B, port, R, Cc, weighted):
     g, u = I.normal(1, (R, Cc), 0, 1.5), I.normal(2, (R, Cc), 0, 1.5)
     rw = I.rng(3).uniform(0, 1, R).astype(np.float32) if weighted else None
