@@ -347,6 +347,15 @@ def main():
     if args.impl == "reference":
         return run_reference(args, rank, world)
     args.warmup = max(args.warmup, 3)
+    # Only the JSON line may reach stdout: libraries (NCCL's banner, CUDA
+    # messages) write to fd 1 directly, so fd 1 is pointed at stderr and the
+    # line is written to a duplicate of the original stdout.
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+
+    def emit(obj):
+        os.write(json_fd, (json.dumps(obj) + "\n").encode())
 
     import torch
 
@@ -354,6 +363,9 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
+        # rank 0's stdout must carry only the JSON line (NCCL's version banner
+        # goes to stdout at INFO/VERSION level)
+        os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     os.environ["DS3_CUDA_PDL"] = str(args.pdl)
     from qw3_b200 import ds3
@@ -378,7 +390,7 @@ def main():
         peak, _ = measured_peak()
         cfg = run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_host)
         if rank == 0:
-            print(json.dumps({"configs": cfg}), flush=True)
+            emit({"configs": cfg})
         return 0
     params_host = make_params()
     P = {"table": ds3.buffer_from_mmap(table_host)}
@@ -472,7 +484,7 @@ def main():
     for g in graphs:
         ds3.graph_free(g)
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         torch.distributed.destroy_process_group()
     return 0

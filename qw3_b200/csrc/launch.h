@@ -32,6 +32,23 @@ cudaError_t launch_k(const LaunchCtx &c, void (*k)(KArgs...), dim3 grid, dim3 bl
     return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
 }
 
+// Same, with `smem` bytes of dynamic shared memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ks(const LaunchCtx &c, void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = c.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = c.pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
 // x [rows, n] (+ r) -> sum_out (optional), norm_out. r == nullptr: plain RMSNorm.
 cudaError_t launch_add_rms_norm(const LaunchCtx &c, const float *x, const float *r, const float *w,
                                 float *sum_out, float *norm_out, int n, int64_t rows, float eps);

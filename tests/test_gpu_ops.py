@@ -218,12 +218,12 @@ def test_qk_norm_rope_shapes(ds3, B, port, nq, nk, hd):
         assert_close(f32(kb, ds3, k.shape), ko, what="k")
 
 
-def test_qk_norm_rope_fp16_storage(ds3, B, port):
-    T = 128
+@pytest.mark.parametrize("T", [128, 2049])
+def test_qk_norm_rope_fp16_storage(ds3, B, port, T):
     q = I.normal(7, (T, 32, 128)).astype(np.float16)
     k = I.normal(8, (T, 4, 128)).astype(np.float16)
     qw, kw = I.gamma(128, 9), I.gamma(128, 10)
-    pos = np.arange(T, dtype=np.int32) * 250
+    pos = (np.arange(T, dtype=np.int32) * 250) % 32768
     qb, kb = B.up(q), B.up(k)
     assert ds3.qk_norm_rope(qb, kb, B.up(qw), B.up(kw), B.up(pos), T, 32, 4, 128, 1e6, 1e-6, F16) == 0
     qo, ko = port.qk_norm_rope(q.astype(np.float32), k.astype(np.float32), qw, kw, pos, 1e6, 1e-6)
