@@ -735,6 +735,32 @@ def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k):
     fn = [lambda: ds3.qk_norm_rope(q16, k16, qw, kw, pos, n, NQ, NK, HD, I.ROPE_THETA, eps, ds3.TYPE_F16)]
     rec("c5_qk_norm_rope_f16_T32768", n, n * (4 * (NQ + NK) * HD + 4), time_launches(ds3, fn, 20, max_over_ranks, barrier))
 
+    # Next-row kernel: QK-norm + RoPE with the fp16 KV-cache write fused in,
+    # against the two launches it replaces (qk_norm_rope + kv_cache_write_batch
+    # on the rotated k and v), at the chunk size and at T=32768 (sharded).
+    for tk in (512, n):
+        msq = max(tk, 4096)
+        qv, kv_, vv = empty(tk * NQ * HD * 4), empty(tk * NK * HD * 4), empty(tk * NK * HD * 4)
+        ds3.buffer_write(qv, 0, I.normal(5100, (tk, NQ, HD)))
+        ds3.buffer_write(kv_, 0, I.normal(5101, (tk, NK, HD)))
+        ds3.buffer_write(vv, 0, I.normal(5102, (tk, NK, HD)))
+        kc, vc = empty(msq * NK * HD * 2), empty(msq * NK * HD * 2)
+        pk = up(np.arange(tk, dtype=np.int32))
+        fused = [lambda: ds3.qk_norm_rope_kv(qv, kv_, vv, qw, kw, pk, kc, vc, tk, NQ, NK, HD, msq, I.ROPE_THETA, eps)]
+        fb = tk * (8 * (NQ + NK) * HD + 4 + 4 * NK * HD + 2 * 2 * NK * HD)
+        rec(f"qk_norm_rope_kv_write_T{tk}", tk, fb, time_launches(ds3, fused, 20, max_over_ranks, barrier),
+            note="fused: q/k in place + fp16 K/V cache rows")
+
+        def two():
+            ds3.qk_norm_rope(qv, kv_, qw, kw, pk, tk, NQ, NK, HD, I.ROPE_THETA, eps)
+            ds3.kv_cache_write_batch(kv_, vv, kc, vc, 0, tk, msq, NQ, NK, HD)
+
+        rec(f"qk_norm_rope_then_kv_write_T{tk}", tk, fb, time_launches(ds3, [two], 20, max_over_ranks, barrier),
+            note="unfused reference sequence, same algorithmic bytes")
+        for x in (qv, kv_, vv, kc, vc):
+            x.free()
+        bufs = [x for x in bufs if x not in (qv, kv_, vv, kc, vc)]
+
     # C2: decode batch of 64 tokens x 48 layers, one graph (per-layer inputs distinct).
     L, B2 = 48, 64
     hid = empty(L * B2 * H * 4)

@@ -156,6 +156,13 @@ int ds3_cuda_moe_router_topk_batch_tokens(const ds3_cuda_buffer_t *logits,
                                           uint32_t n_expert, uint32_t n_used,
                                           bool norm_topk_prob);
 
+/* ds3_metal.h:280-290. k, v fp32 [n_tokens][n_kv_heads][head_dim] -> fp16 cache
+ * rows seq_pos .. seq_pos+n_tokens-1 of [max_seq_len][n_kv_heads][head_dim]. */
+int ds3_cuda_kv_cache_write_batch(const ds3_cuda_buffer_t *k, const ds3_cuda_buffer_t *v,
+                                  ds3_cuda_buffer_t *k_cache, ds3_cuda_buffer_t *v_cache,
+                                  uint32_t seq_pos, uint32_t n_tokens, uint32_t max_seq_len,
+                                  uint32_t n_q_heads, uint32_t n_kv_heads, uint32_t head_dim);
+
 /* ds3_metal.h:457-462. begin_batch returns -1 if a batch is already open. */
 int  ds3_cuda_begin_batch(void);
 int  ds3_cuda_end_batch(void);
@@ -208,6 +215,22 @@ int ds3_cuda_qk_norm_rope(ds3_cuda_buffer_t *q, ds3_cuda_buffer_t *k,
                           uint32_t n_rows, uint32_t n_q_heads, uint32_t n_kv_heads,
                           uint32_t head_dim, float theta_base, float eps,
                           ds3_type_t storage);
+
+/* new: qk_norm_rope plus the KV-cache write of the same tokens, in one pass.
+ * Replaces qk_norm_rope followed by kv_cache_write_batch (ds3_metal.h:280-290):
+ * after q and k are normed and rotated in place, the rotated k rows and the v
+ * rows (v [n_rows, n_kv_heads, 128], `storage` type, not modified) are
+ * written, rounded to fp16, into k_cache / v_cache
+ * [max_seq_len][n_kv_heads][128] at row positions[t]. head_dim must be 128;
+ * a position outside [0, max_seq_len) skips that row's cache write and makes
+ * the call return -1. */
+int ds3_cuda_qk_norm_rope_kv(ds3_cuda_buffer_t *q, ds3_cuda_buffer_t *k, const ds3_cuda_buffer_t *v,
+                             const ds3_cuda_buffer_t *q_w, const ds3_cuda_buffer_t *k_w,
+                             const ds3_cuda_buffer_t *positions,
+                             ds3_cuda_buffer_t *k_cache, ds3_cuda_buffer_t *v_cache,
+                             uint32_t n_rows, uint32_t n_q_heads, uint32_t n_kv_heads,
+                             uint32_t head_dim, uint32_t max_seq_len,
+                             float theta_base, float eps, ds3_type_t storage);
 
 /* Router softmax + top-k + renorm, one warp per token (the Metal kernel is
  * one thread per token, metal/moe.metal:566-624). logits [n_tokens, n_expert];

@@ -48,6 +48,7 @@ _PORT_ONLY = {
     "scatter_add_weighted": (None, [_P, _P, _P, _P, _I64, _I64, _I64]),
     "gather_rows": (None, [_P, _P, _P, _I64, _I64, _I64]),
     "fp16_to_fp32": (_F, [C.c_uint16]),
+    "kv_cache_write": (None, [_P, _P, _P, _I64, _I64, _I64, _P, _P]),
 }
 
 
@@ -171,6 +172,17 @@ class Oracle:
         yr = None if y_rows is None else _arr(y_rows, np.int32)
         self._moe_combine_residual(_p(y), _p(yr), _p(w), _p(residual), _p(out), T, K, Cc, nthreads)
         return out
+
+
+def kv_cache_write(O: Oracle, k, v, cache_k, cache_v, seq_pos=0, row_of=None):
+    """Port oracle only: writes fp16 rows of k/v ([T, n_kv, hd] fp32) into the
+    uint16 caches ([max_seq, n_kv, hd]) in place."""
+    k, v = _arr(k, np.float32), _arr(v, np.float32)
+    T = k.shape[0]
+    row = k.size // max(T, 1)
+    ro = None if row_of is None else _arr(row_of, np.int32)
+    assert cache_k.dtype == np.uint16 and cache_k.flags["C_CONTIGUOUS"] and cache_v.flags["C_CONTIGUOUS"]
+    O._kv_cache_write(_p(k), _p(v), _p(ro), seq_pos, T, row, _p(cache_k), _p(cache_v))
 
 
 _port = None

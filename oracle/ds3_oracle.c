@@ -412,3 +412,18 @@ void ds3o_gather_rows(const float *src, const int32_t *ids, float *dst, int64_t 
         memcpy(dst + i * n_cols, src + (int64_t)ids[offset + i] * n_cols,
                (size_t)n_cols * sizeof(float));
 }
+
+/* kv_cache_write_batch, metal/attention.metal:66-87 (and ds3_metal.m:1588-1660):
+ * k_cache[(seq_pos + t) * row + e] = half(k[t * row + e]), same for v. The
+ * engine's cache is fp16 (src/ds3.h:179-182); conversion rounds to nearest. */
+void ds3o_kv_cache_write(const float *k, const float *v, const int32_t *row_of, int64_t seq_pos,
+                         int64_t n_tokens, int64_t row_elems, uint16_t *k_cache, uint16_t *v_cache)
+{
+    for (int64_t t = 0; t < n_tokens; t++) {
+        const int64_t dst = (row_of ? (int64_t)row_of[t] : seq_pos + t) * row_elems;
+        for (int64_t e = 0; e < row_elems; e++) {
+            k_cache[dst + e] = ds3o_fp32_to_fp16(k[t * row_elems + e]);
+            v_cache[dst + e] = ds3o_fp32_to_fp16(v[t * row_elems + e]);
+        }
+    }
+}

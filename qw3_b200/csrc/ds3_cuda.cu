@@ -730,6 +730,70 @@ int ds3_cuda_qk_norm_rope(ds3_cuda_buffer_t *q, ds3_cuda_buffer_t *k, const ds3_
                   ps);
 }
 
+int ds3_cuda_qk_norm_rope_kv(ds3_cuda_buffer_t *q, ds3_cuda_buffer_t *k, const ds3_cuda_buffer_t *v,
+                             const ds3_cuda_buffer_t *q_w, const ds3_cuda_buffer_t *k_w,
+                             const ds3_cuda_buffer_t *positions, ds3_cuda_buffer_t *k_cache,
+                             ds3_cuda_buffer_t *v_cache, uint32_t n_rows, uint32_t n_q_heads, uint32_t n_kv_heads,
+                             uint32_t head_dim, uint32_t max_seq_len, float theta_base, float eps, ds3_type_t storage)
+{
+    const char *op = "qk_norm_rope_kv";
+    if (!ready(op)) return -1;
+    if ((int)storage != 0 && (int)storage != 1) {
+        set_error("%s: storage must be DS3_TYPE_F32 or DS3_TYPE_F16", op);
+        return -1;
+    }
+    if (head_dim != 128 || n_kv_heads == 0 || max_seq_len == 0) {
+        set_error("%s: needs head_dim 128 (got %u), n_kv_heads > 0, max_seq_len > 0", op, head_dim);
+        return -1;
+    }
+    const size_t es = (int)storage == 1 ? 2 : 4;
+    const size_t qb = (size_t)n_rows * n_q_heads * 128 * es, kb = (size_t)n_rows * n_kv_heads * 128 * es;
+    const size_t cb = (size_t)max_seq_len * n_kv_heads * 128 * 2;
+    if (!need(op, "q", q, qb) || !writable(op, "q", q) || !need(op, "k", k, kb) || !writable(op, "k", k) ||
+        !need(op, "v", v, kb) || !need(op, "q_w", q_w, 512) || !need(op, "k_w", k_w, 512) ||
+        !need(op, "positions", positions, (size_t)n_rows * 4) || !need(op, "k_cache", k_cache, cb) ||
+        !writable(op, "k_cache", k_cache) || !need(op, "v_cache", v_cache, cb) || !writable(op, "v_cache", v_cache))
+        return -1;
+    float freq[256];
+    rope_freqs(head_dim, theta_base, freq);
+    ProfScope ps(op);
+    const cudaError_t e = ds3::launch_qk_norm_rope_kv(
+        ctx(), dptr(q), dptr(k), dptr(v), (const float *)dptr(q_w), (const float *)dptr(k_w),
+        (const int32_t *)dptr(positions), n_rows, (int)n_q_heads, (int)n_kv_heads, freq, eps, (int)storage,
+        dptr(k_cache), dptr(v_cache), (int)max_seq_len);
+    if (e == cudaErrorInvalidValue) {
+        set_error("%s: buffers must be 16-byte aligned and n_q_heads + 2*n_kv_heads <= 40", op);
+        ps.close();
+        return -1;
+    }
+    return finish(op, e, ps);
+}
+
+int ds3_cuda_kv_cache_write_batch(const ds3_cuda_buffer_t *k, const ds3_cuda_buffer_t *v, ds3_cuda_buffer_t *k_cache,
+                                  ds3_cuda_buffer_t *v_cache, uint32_t seq_pos, uint32_t n_tokens,
+                                  uint32_t max_seq_len, uint32_t n_q_heads, uint32_t n_kv_heads, uint32_t head_dim)
+{
+    const char *op = "kv_cache_write_batch";
+    (void)n_q_heads;
+    if (!ready(op)) return -1;
+    if (n_tokens == 0) return 0;
+    if ((uint64_t)seq_pos + n_tokens > max_seq_len) {
+        set_error("%s: seq_pos=%u n_tokens=%u exceeds max_seq_len=%u", op, seq_pos, n_tokens, max_seq_len);
+        return -1;
+    }
+    const size_t row = (size_t)n_kv_heads * head_dim;
+    const size_t cb = (size_t)max_seq_len * row * 2;
+    if (row == 0 || !need(op, "k", k, n_tokens * row * 4) || !need(op, "v", v, n_tokens * row * 4) ||
+        !need(op, "k_cache", k_cache, cb) || !writable(op, "k_cache", k_cache) || !need(op, "v_cache", v_cache, cb) ||
+        !writable(op, "v_cache", v_cache))
+        return -1;
+    ProfScope ps(op);
+    return finish(op,
+                  ds3::launch_kv_cache_write(ctx(), (const float *)dptr(k), (const float *)dptr(v), dptr(k_cache),
+                                             dptr(v_cache), seq_pos, n_tokens, (int64_t)row),
+                  ps);
+}
+
 int ds3_cuda_router_softmax_topk(const ds3_cuda_buffer_t *logits, ds3_cuda_buffer_t *probs_out,
                                  ds3_cuda_buffer_t *idx, ds3_cuda_buffer_t *scores, uint32_t n_tokens,
                                  uint32_t n_expert, uint32_t n_used, bool norm_topk_prob)

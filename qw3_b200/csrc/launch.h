@@ -66,6 +66,16 @@ cudaError_t launch_qk_norm_rope(const LaunchCtx &c, const void *q_src, void *q_d
                                 int nk, int hd, const float *freq, float eps, int do_norm,
                                 int storage);
 
+// qk_norm_rope in place plus fp16 KV-cache rows at positions[t] (head_dim 128).
+cudaError_t launch_qk_norm_rope_kv(const LaunchCtx &c, void *q, void *k, const void *v, const float *q_w,
+                                   const float *k_w, const int32_t *pos, int64_t rows, int nq, int nk,
+                                   const float *freq, float eps, int storage, void *k_cache, void *v_cache,
+                                   int max_seq);
+
+// fp32 k/v [n_tokens][row_elems] -> fp16 cache rows seq_pos.. (row_elems = n_kv_heads * head_dim).
+cudaError_t launch_kv_cache_write(const LaunchCtx &c, const float *k, const float *v, void *k_cache,
+                                  void *v_cache, int64_t seq_pos, int64_t n_tokens, int64_t row_elems);
+
 cudaError_t launch_router_topk(const LaunchCtx &c, const float *logits, float *probs_out,
                                int32_t *idx, float *scores, int64_t n_tokens, int n_expert,
                                int n_used, int norm_topk);

@@ -112,14 +112,42 @@ struct HeadSlice<__half> {
 // the RMS sum is 3 shuffles and the rotation needs no data exchange.
 constexpr int kTileTok = 2;
 constexpr int kTileWarps = 9;
-constexpr int kMaxGroupsPerWarp = 2;  // 2 tokens x 36 heads = 18 groups = 9 warps x 2
 
-template <typename T>
-__global__ void __launch_bounds__(kTileWarps * 32, sizeof(T) == 2 ? 4 : 3) qk_norm_rope_tile(
+// fp16 copy of a lane's 16 values into a 128-wide cache row, at the element
+// positions HeadSlice<T> uses for that lane.
+__device__ __forceinline__ void cache_store(__half *row, int j, const float *lo, const float *hi, float)
+{
+    uint2 *r = reinterpret_cast<uint2 *>(row);
+    auto pk = [](float a, float b, float c, float d) {
+        __half2 x = __floats2half2_rn(a, b), y = __floats2half2_rn(c, d);
+        return make_uint2(*reinterpret_cast<unsigned *>(&x), *reinterpret_cast<unsigned *>(&y));
+    };
+    r[j] = pk(lo[0], lo[1], lo[2], lo[3]);            // elements 4j..4j+3
+    r[8 + j] = pk(lo[4], lo[5], lo[6], lo[7]);        // 32+4j..
+    r[16 + j] = pk(hi[0], hi[1], hi[2], hi[3]);       // 64+4j..
+    r[24 + j] = pk(hi[4], hi[5], hi[6], hi[7]);       // 96+4j..
+}
+__device__ __forceinline__ void cache_store(__half *row, int j, const float *lo, const float *hi, __half)
+{
+    HeadSlice<__half>::store(row, j, lo, hi);
+}
+
+// KV = true additionally handles the V heads of each token (no norm, no
+// rotation) and writes the rotated K rows and the V rows, rounded to fp16,
+// into the KV cache at row positions[t] ([max_seq][n_kv_heads][128]).
+// Warps per CTA: 9 (18 groups of 4 heads for 2 tokens x 36 heads, 2 per
+// warp); with V, 2 x 40 heads = 20 groups over 10 warps, still 2 per warp.
+template <bool KV>
+__host__ __device__ constexpr int tile_warps() { return KV ? 10 : 9; }
+
+template <typename T, bool KV>
+__global__ void __launch_bounds__(tile_warps<KV>() * 32, (sizeof(T) == 2 && !KV) ? 4 : 3) qk_norm_rope_tile(
     const T *q_src, T *q_dst, const T *k_src, T *k_dst, const float *q_w, const float *k_w,
     const int32_t *pos, int64_t rows, int nq, int nk, const __grid_constant__ FreqTable ft, float eps,
-    int do_norm)
+    int do_norm, const T *v_src, __half *k_cache, __half *v_cache, int max_seq, unsigned *err)
 {
+    constexpr int kMaxG = 2;
+    constexpr int kW = tile_warps<KV>();
     __shared__ __align__(16) float cs[kTileTok][64];
     __shared__ __align__(16) float sn[kTileTok][64];
     __shared__ __align__(16) float wq[128];
@@ -137,28 +165,40 @@ __global__ void __launch_bounds__(kTileWarps * 32, sizeof(T) == 2 ? 4 : 3) qk_no
     const int lane = tid & 31, warp = tid >> 5;
     const int sub = lane >> 3;  // head within the group of 4
     const int j = lane & 7;     // slice of the head
-    const int nh = nq + nk;
+    const int nh = nq + nk + (KV ? nk : 0);
     const int n_heads = kTileTok * nh;
     const int n_groups = (n_heads + 3) >> 2;
 
-    float lo[kMaxGroupsPerWarp][8], hi[kMaxGroupsPerWarp][8];
-    T *headp[kMaxGroupsPerWarp];
-    int meta[kMaxGroupsPerWarp];  // bit 0: active, bit 1: K head, bits 2+: local token
+    float lo[kMaxG][8], hi[kMaxG][8];
+    T *headp[kMaxG];
+    __half *cachep[kMaxG];
+    int meta[kMaxG];  // bit 0: active, bit 1: K head, bit 2: V head, bits 3+: local token
 #pragma unroll
-    for (int gi = 0; gi < kMaxGroupsPerWarp; gi++) {
-        const int g = warp + gi * kTileWarps;
+    for (int gi = 0; gi < kMaxG; gi++) {
+        const int g = warp + gi * kW;
         const int h = 4 * g + sub;
         meta[gi] = 0;
         headp[gi] = nullptr;
+        cachep[gi] = nullptr;
         if (g < n_groups && h < n_heads) {
             const int tl = h / nh, hh = h - tl * nh;
             const int64_t t = t0 + tl;
             if (t < rows) {
-                const bool is_k = hh >= nq;
-                const int64_t off = is_k ? (t * nk + (hh - nq)) * 128 : (t * nq + hh) * 128;
-                headp[gi] = (is_k ? k_dst : q_dst) + off;
-                meta[gi] = 1 | (is_k ? 2 : 0) | (tl << 2);
-                HeadSlice<T>::load((is_k ? k_src : q_src) + off, j, lo[gi], hi[gi]);
+                const bool is_v = KV && hh >= nq + nk;
+                const bool is_k = !is_v && hh >= nq;
+                const int kvh = is_v ? hh - nq - nk : hh - nq;
+                const int64_t off = (is_k || is_v) ? (t * nk + kvh) * 128 : (t * nq + hh) * 128;
+                headp[gi] = is_v ? nullptr : (is_k ? k_dst : q_dst) + off;
+                meta[gi] = 1 | (is_k ? 2 : 0) | (is_v ? 4 : 0) | (tl << 3);
+                HeadSlice<T>::load((is_v ? v_src : is_k ? k_src : q_src) + off, j, lo[gi], hi[gi]);
+                if (KV && (is_k || is_v)) {
+                    const int p = pos[t];
+                    if (p >= 0 && p < max_seq) {
+                        cachep[gi] = (is_v ? v_cache : k_cache) + ((int64_t)p * nk + kvh) * 128;
+                    } else if (j == 0) {
+                        flag_error(err, kErrBadId);
+                    }
+                }
             }
         }
         if (!(meta[gi] & 1)) {
@@ -179,9 +219,10 @@ __global__ void __launch_bounds__(kTileWarps * 32, sizeof(T) == 2 ? 4 : 3) qk_no
     __syncthreads();
 
 #pragma unroll
-    for (int gi = 0; gi < kMaxGroupsPerWarp; gi++) {
-        if (warp + gi * kTileWarps >= n_groups) break;  // warp-uniform
+    for (int gi = 0; gi < kMaxG; gi++) {
+        if (warp + gi * kW >= n_groups) break;  // warp-uniform
         float *xl = lo[gi], *xh = hi[gi];
+        const bool is_v = meta[gi] & 4;
         if (do_norm) {
             float ss = 0.0f;
 #pragma unroll
@@ -191,23 +232,26 @@ __global__ void __launch_bounds__(kTileWarps * 32, sizeof(T) == 2 ? 4 : 3) qk_no
             ss += __shfl_xor_sync(kFull, ss, 4);
             const float inv = rms_inv_pow2<128>(ss, eps);
             const float *w = (meta[gi] & 2) ? wk : wq;
+            if (!is_v) {
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-                const int pi = HeadSlice<T>::pidx(j, e);
-                xl[e] = norm_mul(xl[e], inv, w[pi]);
-                xh[e] = norm_mul(xh[e], inv, w[pi + 64]);
+                for (int e = 0; e < 8; e++) {
+                    const int pi = HeadSlice<T>::pidx(j, e);
+                    xl[e] = norm_mul(xl[e], inv, w[pi]);
+                    xh[e] = norm_mul(xh[e], inv, w[pi + 64]);
+                }
             }
         }
-        const int tl = meta[gi] >> 2;
+        const int tl = meta[gi] >> 3;
         float yl[8], yh[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) {
             const int pi = HeadSlice<T>::pidx(j, e);
             const float c = cs[tl][pi], s = sn[tl][pi];
-            yl[e] = rot_lo(xl[e], xh[e], c, s);  // x0*c - x1*s
-            yh[e] = rot_hi(xh[e], xl[e], c, s);  // x0*s + x1*c
+            yl[e] = is_v ? xl[e] : rot_lo(xl[e], xh[e], c, s);  // x0*c - x1*s
+            yh[e] = is_v ? xh[e] : rot_hi(xh[e], xl[e], c, s);  // x0*s + x1*c
         }
-        if (meta[gi] & 1) HeadSlice<T>::store(headp[gi], j, yl, yh);
+        if (headp[gi]) HeadSlice<T>::store(headp[gi], j, yl, yh);
+        if (KV && cachep[gi]) cache_store(cachep[gi], j, yl, yh, T());
     }
 }
 
@@ -479,8 +523,9 @@ cudaError_t run(const LaunchCtx &c, const void *qs, void *qd, const void *ks, vo
 {
     if (use_hd128) {
         const int64_t blocks = (rows + kTileTok - 1) / kTileTok;
-        launch_k(c, qk_norm_rope_tile<T>, dim3((unsigned)blocks), dim3(kTileWarps * 32), (const T *)qs, (T *)qd,
-                 (const T *)ks, (T *)kd, q_w, k_w, pos, rows, nq, nk, ft, eps, do_norm);
+        launch_k(c, qk_norm_rope_tile<T, false>, dim3((unsigned)blocks), dim3(kTileWarps * 32), (const T *)qs,
+                 (T *)qd, (const T *)ks, (T *)kd, q_w, k_w, pos, rows, nq, nk, ft, eps, do_norm, (const T *)nullptr,
+                 (__half *)nullptr, (__half *)nullptr, 0, c.err);
     } else {
         dim3 grid((unsigned)rows, (unsigned)(nq + nk));
         const int threads = ((hd / 2 + 31) / 32) * 32;
@@ -510,7 +555,7 @@ cudaError_t launch_qk_norm_rope(const LaunchCtx &c, const void *q_src, void *q_d
                            reinterpret_cast<uintptr_t>(k_src) | reinterpret_cast<uintptr_t>(k_dst);
     const uintptr_t wts = reinterpret_cast<uintptr_t>(q_w) | reinterpret_cast<uintptr_t>(k_w);
     const int groups = (kTileTok * (nq + nk) + 3) / 4;
-    const int use_hd = (hd == 128 && (data & m) == 0 && groups <= kTileWarps * kMaxGroupsPerWarp) ? 128 : 0;
+    const int use_hd = (hd == 128 && (data & m) == 0 && groups <= kTileWarps * 2) ? 128 : 0;
     (void)wts;
     // fp16 storage at large token counts: the TMA-staged kernel (measured at
     // T=32768: 126 us vs 138 us for the register-tile kernel; fp32 is faster
@@ -526,6 +571,61 @@ cudaError_t launch_qk_norm_rope(const LaunchCtx &c, const void *q_src, void *q_d
                            do_norm);
     return run<float>(c, q_src, q_dst, k_src, k_dst, q_w, k_w, pos, rows, nq, nk, hd, use_hd, ft, eps,
                       do_norm);
+}
+
+cudaError_t launch_qk_norm_rope_kv(const LaunchCtx &c, void *q, void *k, const void *v, const float *q_w,
+                                   const float *k_w, const int32_t *pos, int64_t rows, int nq, int nk,
+                                   const float *freq, float eps, int storage, void *k_cache, void *v_cache,
+                                   int max_seq)
+{
+    if (rows <= 0) return cudaSuccess;
+    const int groups = (kTileTok * (nq + 2 * nk) + 3) / 4;
+    constexpr int kW = tile_warps<true>();
+    const uintptr_t al = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                         reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(k_cache) |
+                         reinterpret_cast<uintptr_t>(v_cache);
+    if ((al & 15u) || groups > kW * 2 || rows > 0x7fffffffLL) return cudaErrorInvalidValue;
+    FreqTable ft;
+    for (int i = 0; i < 64; i++) ft.f[i] = freq[i];
+    const int64_t blocks = (rows + kTileTok - 1) / kTileTok;
+    if (storage)
+        launch_k(c, qk_norm_rope_tile<__half, true>, dim3((unsigned)blocks), dim3(kW * 32),
+                 (const __half *)q, (__half *)q, (const __half *)k, (__half *)k, q_w, k_w, pos, rows, nq, nk, ft, eps,
+                 1, (const __half *)v, (__half *)k_cache, (__half *)v_cache, max_seq, c.err);
+    else
+        launch_k(c, qk_norm_rope_tile<float, true>, dim3((unsigned)blocks), dim3(kW * 32),
+                 (const float *)q, (float *)q, (const float *)k, (float *)k, q_w, k_w, pos, rows, nq, nk, ft, eps, 1,
+                 (const float *)v, (__half *)k_cache, (__half *)v_cache, max_seq, c.err);
+    return cudaGetLastError();
+}
+
+namespace {
+// KV-cache write of a chunk, metal/attention.metal:66-87: row seq_pos + t of
+// the fp16 cache [max_seq][n_kv_heads][head_dim] gets half(k[t]), half(v[t]).
+__global__ void kv_cache_write_k(const float *k, const float *v, __half *kc, __half *vc, int64_t seq_pos,
+                                 int64_t n_elems, int64_t row_elems)
+{
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_elems;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t dst = seq_pos * row_elems + e;
+        kc[dst] = __float2half_rn(k[e]);
+        vc[dst] = __float2half_rn(v[e]);
+    }
+}
+}  // namespace
+
+cudaError_t launch_kv_cache_write(const LaunchCtx &c, const float *k, const float *v, void *k_cache,
+                                  void *v_cache, int64_t seq_pos, int64_t n_tokens, int64_t row_elems)
+{
+    const int64_t n = n_tokens * row_elems;
+    if (n <= 0) return cudaSuccess;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > (int64_t)c.n_sm * 16) blocks = (int64_t)c.n_sm * 16;
+    launch_k(c, kv_cache_write_k, dim3((unsigned)blocks), dim3(256), k, v, (__half *)k_cache, (__half *)v_cache,
+             seq_pos, n, row_elems);
+    return cudaGetLastError();
 }
 
 }  // namespace ds3

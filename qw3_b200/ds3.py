@@ -69,6 +69,8 @@ _SIGS = {
     "add_rms_norm": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _F]),
     "qk_norm_rope": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _F, _F, _I]),
     "router_softmax_topk": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _B]),
+    "qk_norm_rope_kv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _F, _F, _I]),
+    "kv_cache_write_batch": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32]),
     "swiglu": (_I, [_P, _P, _P, _P, _U32, _U32]),
     "moe_combine_residual": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32]),
     "stream": (_P, []),
@@ -297,6 +299,19 @@ def qk_norm_rope(q, k, q_w, k_w, positions, n_rows, n_q_heads, n_kv_heads, head_
                  storage=TYPE_F32) -> int:
     return lib().ds3_cuda_qk_norm_rope(_h(q), _h(k), _h(q_w), _h(k_w), _h(positions), n_rows, n_q_heads,
                                        n_kv_heads, head_dim, theta_base, eps, storage)
+
+
+def qk_norm_rope_kv(q, k, v, q_w, k_w, positions, k_cache, v_cache, n_rows, n_q_heads, n_kv_heads, head_dim,
+                    max_seq_len, theta_base, eps, storage=TYPE_F32) -> int:
+    return lib().ds3_cuda_qk_norm_rope_kv(_h(q), _h(k), _h(v), _h(q_w), _h(k_w), _h(positions), _h(k_cache),
+                                          _h(v_cache), n_rows, n_q_heads, n_kv_heads, head_dim, max_seq_len,
+                                          theta_base, eps, storage)
+
+
+def kv_cache_write_batch(k, v, k_cache, v_cache, seq_pos, n_tokens, max_seq_len, n_q_heads, n_kv_heads,
+                         head_dim) -> int:
+    return lib().ds3_cuda_kv_cache_write_batch(_h(k), _h(v), _h(k_cache), _h(v_cache), seq_pos, n_tokens,
+                                               max_seq_len, n_q_heads, n_kv_heads, head_dim)
 
 
 def router_softmax_topk(logits, probs_out, idx, scores, n_tokens, n_expert, n_used, norm_topk_prob) -> int:

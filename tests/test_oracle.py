@@ -262,3 +262,18 @@ def test_reference_own_known_answer_program():
     res = subprocess.run([str(exe)], capture_output=True, text=True)
     assert res.returncode == 0, res.stdout[-2000:]
     assert "0 failed" in res.stdout
+
+
+def test_kv_cache_write_rounds_like_numpy_fp16(port):
+    # metal/attention.metal:66-87 stores half(k), half(v) at row seq_pos + t.
+    k = I.normal(30, (3, 4, 128), 0.0, 3.0)
+    v = I.normal(31, (3, 4, 128), 0.0, 3.0)
+    ck = np.full((9, 4, 128), 0x7E00, np.uint16)
+    cv = ck.copy()
+    oracle.kv_cache_write(port, k, v, ck, cv, seq_pos=5)
+    assert np.array_equal(ck[5:8].view(np.float16), k.astype(np.float16))
+    assert np.array_equal(cv[5:8].view(np.float16), v.astype(np.float16))
+    assert (ck[:5] == 0x7E00).all() and (ck[8:] == 0x7E00).all()
+    rows = np.array([8, 0, 3], np.int32)
+    oracle.kv_cache_write(port, k, v, ck, cv, row_of=rows)
+    assert np.array_equal(ck[rows].view(np.float16), k.astype(np.float16))
