@@ -761,6 +761,16 @@ def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k):
             x.free()
         bufs = [x for x in bufs if x not in (qv, kv_, vv, kc, vc)]
 
+    # Next-row kernel: device-side per-expert token lists for a 512-token
+    # chunk (replaces the host loop + per-layer index readback of the engine).
+    lg_r = I.normal(5200, (512, E), 0.0, 2.0)
+    ixr, scr = up(np.zeros((512, K), np.int32)), up(np.zeros((512, K), np.float32))
+    ds3.router_softmax_topk(up(lg_r), None, ixr, scr, 512, E, K, True)
+    cnt, lids, lsc, slot = empty(E * 4), empty(E * 512 * 4), empty(E * 512 * 4), empty(512 * K * 4)
+    fn = [lambda: ds3.moe_expert_lists(ixr, scr, cnt, lids, lsc, slot, 512, E, K, 512)]
+    rec("moe_expert_lists_T512", 512, 512 * K * (4 + 4 + 4 + 4 + 4), time_launches(ds3, fn, 20, max_over_ranks, barrier),
+        note="latency-bound permutation, one CTA per expert; bytes: idx, scores in; ids, scores, slot out")
+
     # C2: decode batch of 64 tokens x 48 layers, one graph (per-layer inputs distinct).
     L, B2 = 48, 64
     hid = empty(L * B2 * H * 4)

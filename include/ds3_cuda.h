@@ -242,6 +242,21 @@ int ds3_cuda_router_softmax_topk(const ds3_cuda_buffer_t *logits,
                                  uint32_t n_tokens, uint32_t n_expert, uint32_t n_used,
                                  bool norm_topk_prob);
 
+/* new: per-expert token lists on the device. Replaces the host loop of
+ * forward_chunk_post_gathered (src/ds3_engine.c:933-965) and the per-layer
+ * readback of indices/scores it needs (:1256-1261). idx int32 / scores fp32
+ * [n_tokens, n_used] (router output); counts int32 [n_expert]; ids int32 and
+ * gscores fp32 [n_expert * cap]: the tokens that chose expert ex, ascending,
+ * at ids[ex*cap + j] with their scores, exactly as the engine lays them out
+ * (cap = n_tokens there). slot_of int32 [n_tokens * n_used] (or NULL) gets
+ * ex*cap + j for each (token, slot): pass it as y_rows to
+ * moe_combine_residual to read expert outputs in this layout. Slots past
+ * counts[ex] are not written. n_expert <= 256. */
+int ds3_cuda_moe_expert_lists(const ds3_cuda_buffer_t *idx, const ds3_cuda_buffer_t *scores,
+                              ds3_cuda_buffer_t *counts, ds3_cuda_buffer_t *ids,
+                              ds3_cuda_buffer_t *gscores, ds3_cuda_buffer_t *slot_of,
+                              uint32_t n_tokens, uint32_t n_expert, uint32_t n_used, uint32_t cap);
+
 /* SwiGLU with optional per-row routing weight:
  * out[r][c] = (silu(gate[r][c]) * up[r][c]) * row_weight[r]. row_weight may be
  * NULL (plain silu_mul, metal/moe.metal:95-108). */

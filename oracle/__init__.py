@@ -49,6 +49,7 @@ _PORT_ONLY = {
     "gather_rows": (None, [_P, _P, _P, _I64, _I64, _I64]),
     "fp16_to_fp32": (_F, [C.c_uint16]),
     "kv_cache_write": (None, [_P, _P, _P, _I64, _I64, _I64, _P, _P]),
+    "moe_expert_lists": (_I, [_P, _P, _I64, _I, _I, _I64, _P, _P, _P, _P]),
 }
 
 
@@ -183,6 +184,18 @@ def kv_cache_write(O: Oracle, k, v, cache_k, cache_v, seq_pos=0, row_of=None):
     ro = None if row_of is None else _arr(row_of, np.int32)
     assert cache_k.dtype == np.uint16 and cache_k.flags["C_CONTIGUOUS"] and cache_v.flags["C_CONTIGUOUS"]
     O._kv_cache_write(_p(k), _p(v), _p(ro), seq_pos, T, row, _p(cache_k), _p(cache_v))
+
+
+def moe_expert_lists(O: Oracle, idx, scores, n_expert, cap, fill_ids=-7, fill_scores=np.nan):
+    """Port oracle only: (rc, counts, ids, gscores, slot_of); unwritten slots keep the fill values."""
+    idx, scores = _arr(idx, np.int32), _arr(scores, np.float32)
+    T, K = idx.shape
+    counts = np.zeros(n_expert, np.int32)
+    ids = np.full(n_expert * cap, fill_ids, np.int32)
+    gs = np.full(n_expert * cap, fill_scores, np.float32)
+    slot = np.empty(T * K, np.int32)
+    rc = O._moe_expert_lists(_p(idx), _p(scores), T, K, n_expert, cap, _p(counts), _p(ids), _p(gs), _p(slot))
+    return rc, counts, ids, gs, slot
 
 
 _port = None

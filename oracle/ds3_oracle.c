@@ -427,3 +427,30 @@ void ds3o_kv_cache_write(const float *k, const float *v, const int32_t *row_of, 
         }
     }
 }
+
+/* Per-expert token lists: forward_chunk_post_gathered, src/ds3_engine.c:933-954
+ * (counts zeroed, then for t ascending, k ascending: slot ex*M + counts[ex]++). */
+int ds3o_moe_expert_lists(const int32_t *idx, const float *scores, int64_t n_tokens, int n_used,
+                          int n_expert, int64_t cap, int32_t *counts, int32_t *ids, float *gscores,
+                          int32_t *slot_of)
+{
+    int rc = 0;
+    memset(counts, 0, (size_t)n_expert * sizeof(int32_t));
+    for (int64_t t = 0; t < n_tokens; t++) {
+        for (int k = 0; k < n_used; k++) {
+            const int64_t i = t * n_used + k;
+            const int32_t ex = idx[i];
+            if (ex < 0 || ex >= n_expert || counts[ex] >= cap) {
+                rc = -1;
+                if (slot_of) slot_of[i] = -1;
+                continue;
+            }
+            const int64_t slot = (int64_t)ex * cap + counts[ex];
+            ids[slot] = (int32_t)t;
+            gscores[slot] = scores[i];
+            if (slot_of) slot_of[i] = (int32_t)slot;
+            counts[ex]++;
+        }
+    }
+    return rc;
+}

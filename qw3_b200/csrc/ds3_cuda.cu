@@ -802,6 +802,30 @@ int ds3_cuda_router_softmax_topk(const ds3_cuda_buffer_t *logits, ds3_cuda_buffe
                          norm_topk_prob);
 }
 
+int ds3_cuda_moe_expert_lists(const ds3_cuda_buffer_t *idx, const ds3_cuda_buffer_t *scores, ds3_cuda_buffer_t *counts,
+                              ds3_cuda_buffer_t *ids, ds3_cuda_buffer_t *gscores, ds3_cuda_buffer_t *slot_of,
+                              uint32_t n_tokens, uint32_t n_expert, uint32_t n_used, uint32_t cap)
+{
+    const char *op = "moe_expert_lists";
+    if (!ready(op)) return -1;
+    if (n_expert == 0 || n_expert > 256 || n_used == 0 || cap == 0) {
+        set_error("%s: need 0 < n_expert <= 256, n_used > 0, cap > 0", op);
+        return -1;
+    }
+    const size_t ent = (size_t)n_tokens * n_used * 4, lists = (size_t)n_expert * cap * 4;
+    if (!need(op, "idx", idx, ent) || !need(op, "scores", scores, ent) || !need(op, "counts", counts, n_expert * 4) ||
+        !writable(op, "counts", counts) || !need(op, "ids", ids, lists) || !writable(op, "ids", ids) ||
+        !need(op, "gscores", gscores, lists) || !writable(op, "gscores", gscores) ||
+        (slot_of && (!need(op, "slot_of", slot_of, ent) || !writable(op, "slot_of", slot_of))))
+        return -1;
+    ProfScope ps(op);
+    return finish(op,
+                  ds3::launch_moe_expert_lists(ctx(), (const int32_t *)dptr(idx), (const float *)dptr(scores),
+                                               (int32_t *)dptr(counts), (int32_t *)dptr(ids), (float *)dptr(gscores),
+                                               (int32_t *)dptr(slot_of), n_tokens, (int)n_used, (int)n_expert, cap),
+                  ps);
+}
+
 int ds3_cuda_swiglu(const ds3_cuda_buffer_t *gate, const ds3_cuda_buffer_t *up, const ds3_cuda_buffer_t *row_weight,
                     ds3_cuda_buffer_t *out, uint32_t n_rows, uint32_t n_cols)
 {

@@ -76,6 +76,11 @@ cudaError_t launch_qk_norm_rope_kv(const LaunchCtx &c, void *q, void *k, const v
 cudaError_t launch_kv_cache_write(const LaunchCtx &c, const float *k, const float *v, void *k_cache,
                                   void *v_cache, int64_t seq_pos, int64_t n_tokens, int64_t row_elems);
 
+// Per-expert token lists from top-k (engine layout ids[ex*cap + j]), counts, slot map.
+cudaError_t launch_moe_expert_lists(const LaunchCtx &c, const int32_t *idx, const float *scores, int32_t *counts,
+                                    int32_t *ids, float *gscores, int32_t *slot_of, int64_t n_tokens, int n_used,
+                                    int n_expert, int64_t cap);
+
 cudaError_t launch_router_topk(const LaunchCtx &c, const float *logits, float *probs_out,
                                int32_t *idx, float *scores, int64_t n_tokens, int n_expert,
                                int n_used, int norm_topk);

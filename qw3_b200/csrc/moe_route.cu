@@ -1,0 +1,104 @@
+// Device-side MoE token permutation (sm_100a): per-expert token lists built
+// from the router's top-k on the GPU.
+//
+// Reference: the host loop of forward_chunk_post_gathered
+// (src/ds3_engine.c:933-965), which reads idx/scores back to the host every
+// layer (:1256-1261) and writes, for expert ex, the tokens that chose it to
+// ids[ex * M + j] (j = running count, so tokens in ascending order, each
+// token's k slots in order) and their scores alongside; counts[ex] = j.
+//
+// One CTA per expert, all experts in parallel. CTA ex walks the T*K
+// (token, slot) entries in entry order, 1024 at a time (8 chunks of loads
+// issued before any is used): a ballot gives each warp's hits and each hit's
+// rank, a 32-value warp scan the offsets of earlier warps, and a running base
+// carries over between chunks. Every hit lands at ids[ex*cap + j] in the
+// engine's order, with no atomics and no memory beyond the outputs.
+// slot_of[t*K+k] = ex*cap + j is written by the CTA of the entry's expert; it
+// is the row map moe_combine_residual takes to read expert outputs laid out
+// per expert. CTA 0 also flags entries whose expert id is out of range.
+#include "common.cuh"
+#include "launch.h"
+
+namespace ds3 {
+namespace {
+
+constexpr int kRouteThreads = 1024;
+constexpr int kRouteWarps = kRouteThreads / 32;
+constexpr int kPrefetch = 8;
+
+__global__ void __launch_bounds__(kRouteThreads) moe_expert_lists_k(
+    const int32_t *idx, const float *scores, int32_t *counts, int32_t *ids, float *gscores, int32_t *slot_of,
+    int64_t n_entries, int n_used, int n_expert, int64_t cap, unsigned *err)
+{
+    __shared__ int32_t wpre[kRouteWarps];
+    __shared__ int32_t total;
+    pdl_wait();
+    pdl_trigger();
+    const int ex = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    int64_t base = 0;
+    for (int64_t s0 = 0; s0 < n_entries; s0 += (int64_t)kPrefetch * kRouteThreads) {
+        int ev[kPrefetch];
+#pragma unroll
+        for (int c = 0; c < kPrefetch; c++) {
+            const int64_t i = s0 + (int64_t)c * kRouteThreads + tid;
+            ev[c] = i < n_entries ? idx[i] : -1;
+            if (ex == 0 && i < n_entries && (ev[c] < 0 || ev[c] >= n_expert)) {
+                flag_error(err, kErrBadId);
+                if (slot_of) slot_of[i] = -1;
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < kPrefetch; c++) {
+            const int64_t c0 = s0 + (int64_t)c * kRouteThreads;
+            if (c0 >= n_entries) break;  // uniform across the CTA
+            const bool hit = ev[c] == ex;
+            const unsigned bal = __ballot_sync(kFull, hit);
+            if (lane == 0) wpre[warp] = __popc(bal);
+            __syncthreads();
+            if (warp == 0) {  // exclusive scan of the 32 warp counts
+                const int v = wpre[lane];
+                int inc = v;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(kFull, inc, o);
+                    if (lane >= o) inc += y;
+                }
+                wpre[lane] = inc - v;
+                if (lane == 31) total = inc;
+            }
+            __syncthreads();
+            if (hit) {
+                const int64_t i = c0 + tid;
+                const int64_t j = base + wpre[warp] + __popc(bal & lt_mask);
+                if (j < cap) {
+                    const int64_t slot = (int64_t)ex * cap + j;
+                    ids[slot] = (int32_t)(i / n_used);
+                    gscores[slot] = scores[i];
+                    if (slot_of) slot_of[i] = (int32_t)slot;
+                } else {
+                    flag_error(err, kErrBadId);
+                    if (slot_of) slot_of[i] = -1;
+                }
+            }
+            base += total;
+            __syncthreads();  // wpre / total are rewritten by the next chunk
+        }
+    }
+    if (tid == 0) counts[ex] = (int32_t)base;
+}
+
+}  // namespace
+
+cudaError_t launch_moe_expert_lists(const LaunchCtx &c, const int32_t *idx, const float *scores, int32_t *counts,
+                                    int32_t *ids, float *gscores, int32_t *slot_of, int64_t n_tokens, int n_used,
+                                    int n_expert, int64_t cap)
+{
+    if (n_expert <= 0 || n_expert > 65535) return cudaErrorInvalidValue;
+    launch_k(c, moe_expert_lists_k, dim3((unsigned)n_expert), dim3(kRouteThreads), idx, scores, counts, ids, gscores, slot_of,
+             n_tokens * n_used, n_used, n_expert, cap, c.err);
+    return cudaGetLastError();
+}
+
+}  // namespace ds3

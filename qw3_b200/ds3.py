@@ -72,6 +72,7 @@ _SIGS = {
     "qk_norm_rope_kv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _F, _F, _I]),
     "kv_cache_write_batch": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32]),
     "swiglu": (_I, [_P, _P, _P, _P, _U32, _U32]),
+    "moe_expert_lists": (_I, [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32]),
     "moe_combine_residual": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32]),
     "stream": (_P, []),
     "graph_begin": (_I, []),
@@ -317,6 +318,11 @@ def kv_cache_write_batch(k, v, k_cache, v_cache, seq_pos, n_tokens, max_seq_len,
 def router_softmax_topk(logits, probs_out, idx, scores, n_tokens, n_expert, n_used, norm_topk_prob) -> int:
     return lib().ds3_cuda_router_softmax_topk(_h(logits), _h(probs_out), _h(idx), _h(scores), n_tokens,
                                               n_expert, n_used, bool(norm_topk_prob))
+
+
+def moe_expert_lists(idx, scores, counts, ids, gscores, slot_of, n_tokens, n_expert, n_used, cap) -> int:
+    return lib().ds3_cuda_moe_expert_lists(_h(idx), _h(scores), _h(counts), _h(ids), _h(gscores), _h(slot_of),
+                                           n_tokens, n_expert, n_used, cap)
 
 
 def swiglu(gate, up, row_weight, out, n_rows, n_cols) -> int:

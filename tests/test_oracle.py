@@ -277,3 +277,16 @@ def test_kv_cache_write_rounds_like_numpy_fp16(port):
     rows = np.array([8, 0, 3], np.int32)
     oracle.kv_cache_write(port, k, v, ck, cv, row_of=rows)
     assert np.array_equal(ck[rows].view(np.float16), k.astype(np.float16))
+
+
+def test_moe_expert_lists_engine_layout(port):
+    # src/ds3_engine.c:933-954: tokens ascending per expert, strided by M.
+    idx = np.array([[2, 0], [0, 1], [2, 1]], np.int32)
+    sc = np.array([[0.6, 0.4], [0.7, 0.3], [0.5, 0.5]], np.float32)
+    rc, counts, ids, gs, slot = oracle.moe_expert_lists(port, idx, sc, 3, 3)
+    assert rc == 0 and list(counts) == [2, 2, 2]
+    assert list(ids[0:2]) == [0, 1] and list(ids[3:5]) == [1, 2] and list(ids[6:8]) == [0, 2]
+    assert np.allclose(gs[[0, 1, 3, 4, 6, 7]], [0.4, 0.7, 0.3, 0.5, 0.6, 0.5])
+    assert list(slot) == [6, 0, 1, 3, 7, 4]
+    rc, *_ = oracle.moe_expert_lists(port, np.array([[5, 0]], np.int32), sc[:1], 3, 3)
+    assert rc == -1
