@@ -50,8 +50,10 @@ __device__ __forceinline__ float h2f(const uint8_t *p)
 }
 
 // Q4_K row in shared memory -> this lane's 2*NB float4 (ds3_reference.c:76-113).
-template <int NB>
-__device__ __forceinline__ void unpack_q4k(const uint8_t *rowp, int lane, float4 *out)
+// STORE: write each float4 to dst[k*32 + lane] as soon as it is decoded
+// (nothing held in registers); otherwise return the row in out[].
+template <int NB, bool STORE>
+__device__ __forceinline__ void unpack_q4k(const uint8_t *rowp, int lane, float4 *out, float4 *dst)
 {
     const int hi = (lane >> 3) & 1;  // 0: low nibbles, 1: high nibbles
     const int sh = hi * 4;
@@ -74,10 +76,12 @@ __device__ __forceinline__ void unpack_q4k(const uint8_t *rowp, int lane, float4
         const float d1 = __fmul_rn(d, (float)sc);
         const float m1 = __fmul_rn(dmin, (float)mn);
         const uint32_t q = *reinterpret_cast<const uint32_t *>(blk + 16 + 32 * grp + 4 * (lane & 7));
-        out[k].x = __fsub_rn(__fmul_rn(d1, (float)((q >> (0 + sh)) & 15u)), m1);
-        out[k].y = __fsub_rn(__fmul_rn(d1, (float)((q >> (8 + sh)) & 15u)), m1);
-        out[k].z = __fsub_rn(__fmul_rn(d1, (float)((q >> (16 + sh)) & 15u)), m1);
-        out[k].w = __fsub_rn(__fmul_rn(d1, (float)((q >> (24 + sh)) & 15u)), m1);
+        const float4 r = make_float4(__fsub_rn(__fmul_rn(d1, (float)((q >> (0 + sh)) & 15u)), m1),
+                                     __fsub_rn(__fmul_rn(d1, (float)((q >> (8 + sh)) & 15u)), m1),
+                                     __fsub_rn(__fmul_rn(d1, (float)((q >> (16 + sh)) & 15u)), m1),
+                                     __fsub_rn(__fmul_rn(d1, (float)((q >> (24 + sh)) & 15u)), m1));
+        if constexpr (STORE) dst[k * 32 + lane] = r;
+        else out[k] = r;
     }
 }
 
@@ -88,8 +92,8 @@ __device__ __forceinline__ uint32_t ld_u32_from_u16(const uint8_t *p)
 }
 
 // Q6_K row in shared memory -> this lane's 2*NB float4 (ds3_reference.c:130-158).
-template <int NB>
-__device__ __forceinline__ void unpack_q6k(const uint8_t *rowp, int lane, float4 *out)
+template <int NB, bool STORE>
+__device__ __forceinline__ void unpack_q6k(const uint8_t *rowp, int lane, float4 *out, float4 *dst)
 {
     const int quad = lane >> 3;           // which of q1..q4 (32-weight quarter)
     const int l = 4 * (lane & 7);         // first of 4 positions in the quarter
@@ -110,15 +114,16 @@ __device__ __forceinline__ void unpack_q6k(const uint8_t *rowp, int lane, float4
             const int q = (int)(((lq >> (8 * b + nsh)) & 15u) | (((hq >> (8 * b + hsh)) & 3u) << 4)) - 32;
             v[b] = __fmul_rn(dsc, (float)q);
         }
-        out[k] = make_float4(v[0], v[1], v[2], v[3]);
+        if constexpr (STORE) dst[k * 32 + lane] = make_float4(v[0], v[1], v[2], v[3]);
+        else out[k] = make_float4(v[0], v[1], v[2], v[3]);
     }
 }
 
-template <int TYPE, int NB>
-__device__ __forceinline__ void unpack_row(const uint8_t *rowp, int lane, float4 *out)
+template <int TYPE, int NB, bool STORE>
+__device__ __forceinline__ void unpack_row(const uint8_t *rowp, int lane, float4 *out, float4 *dst)
 {
-    if constexpr (TYPE == kTypeQ4K) unpack_q4k<NB>(rowp, lane, out);
-    else unpack_q6k<NB>(rowp, lane, out);
+    if constexpr (TYPE == kTypeQ4K) unpack_q4k<NB, STORE>(rowp, lane, out, dst);
+    else unpack_q6k<NB, STORE>(rowp, lane, out, dst);
 }
 
 template <int NB>
@@ -144,6 +149,32 @@ __device__ __forceinline__ void emit_row(float4 *v, int lane, int64_t row, float
     }
 }
 
+// Decode one staged row: with a norm, keep it in registers and emit hidden +
+// norm; without, stream each decoded float4 straight to the output row.
+template <int TYPE, int NB, bool NORM>
+__device__ __forceinline__ void decode_row(const uint8_t *rowp, int lane, int64_t row, float *hidden,
+                                           const float *w, float *norm, float eps)
+{
+    if constexpr (NORM) {
+        float4 v[2 * NB];
+        unpack_row<TYPE, NB, false>(rowp, lane, v, nullptr);
+        emit_row<NB>(v, lane, row, hidden, w, norm, eps);
+    } else {
+        unpack_row<TYPE, NB, true>(rowp, lane, nullptr, reinterpret_cast<float4 *>(hidden + row * NB * 256));
+    }
+}
+
+template <int NB>
+__device__ __forceinline__ void zero_row(int lane, int64_t row, float *hidden, float *norm)
+{
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 2 * NB; k++) {
+        if (hidden) reinterpret_cast<float4 *>(hidden + row * NB * 256)[k * 32 + lane] = z;
+        if (norm) reinterpret_cast<float4 *>(norm + row * NB * 256)[k * 32 + lane] = z;
+    }
+}
+
 struct EmbedArgs {
     const uint8_t *table;
     const int32_t *ids;
@@ -158,7 +189,7 @@ struct EmbedArgs {
     int use_bulk;
 };
 
-template <int TYPE, int NB>
+template <int TYPE, int NB, bool NORM>
 __global__ void __launch_bounds__(kWarps * 32) embed_warp(const EmbedArgs a)
 {
     pdl_wait();
@@ -175,24 +206,20 @@ __global__ void __launch_bounds__(kWarps * 32) embed_warp(const EmbedArgs a)
     int64_t cur = (int64_t)blockIdx.x * warps + wid;
     if (cur >= a.n_ids) return;  // whole warp leaves together; no CTA barrier below
 
-    float4 v[2 * NB];
-
     if (!a.use_bulk) {
         // Byte-copy staging: the warp copies the row into its slot, then unpacks.
         for (; cur < a.n_ids; cur += stride) {
             const int32_t id = a.ids[cur];
             if (id < 0 || id >= a.n_vocab) {
                 if (lane == 0) flag_error(a.err, kErrBadId);
-#pragma unroll
-                for (int k = 0; k < 2 * NB; k++) v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                zero_row<NB>(lane, cur, a.hidden, a.norm);
             } else {
                 const uint8_t *src = a.table + (uint64_t)id * a.row_stride;
                 for (int i = lane; i < kRowBytes; i += 32) slots[wid][0][i] = src[i];
                 __syncwarp();
-                unpack_row<TYPE, NB>(slots[wid][0], lane, v);
+                decode_row<TYPE, NB, NORM>(slots[wid][0], lane, cur, a.hidden, a.w, a.norm, a.eps);
                 __syncwarp();
             }
-            emit_row<NB>(v, lane, cur, a.hidden, a.w, a.norm, a.eps);
         }
         return;
     }
@@ -236,14 +263,12 @@ __global__ void __launch_bounds__(kWarps * 32) embed_warp(const EmbedArgs a)
                 if (nxt_ok) mbar_wait(&bars[wid][slot ^ 1], (parity >> (slot ^ 1)) & 1u, kWaitLimit);
                 return;
             }
-            unpack_row<TYPE, NB>(slots[wid][slot], lane, v);
+            decode_row<TYPE, NB, NORM>(slots[wid][slot], lane, cur, a.hidden, a.w, a.norm, a.eps);
             __syncwarp();  // slot free before it is refilled two rows later
         } else {
             if (lane == 0) flag_error(a.err, kErrBadId);
-#pragma unroll
-            for (int k = 0; k < 2 * NB; k++) v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            zero_row<NB>(lane, cur, a.hidden, a.norm);
         }
-        emit_row<NB>(v, lane, cur, a.hidden, a.w, a.norm, a.eps);
         cur = nxt;
         cur_id = nxt_id;
         cur_ok = nxt_ok;
@@ -327,9 +352,14 @@ cudaError_t run_fast(const LaunchCtx &c, const EmbedArgs &a)
     // Few rows: one warp per CTA so the rows spread over every SM.
     const int warps = a.n_ids < 8 * (int64_t)c.n_sm ? 1 : kWarps;
     const int64_t need = (a.n_ids + warps - 1) / warps;
-    const int64_t cap = (int64_t)c.n_sm * 8;
-    const int64_t blocks = need < cap ? need : cap;
-    launch_k(c, embed_warp<TYPE, NB>, dim3((unsigned)blocks), dim3(warps * 32), a);
+    // One row per warp, no persistent grid: the scattered 8 KB output rows
+    // drain best when warps retire and new ones start (measured at T=32768:
+    // Q6_K 52 us vs 56-71 us for one or two resident waves of persistent
+    // warps; Q4_K + norm 89 us vs 99 us). The kernel's two-slot TMA pipeline
+    // still serves any warp that is given more than one row.
+    auto kern = a.norm ? embed_warp<TYPE, NB, true> : embed_warp<TYPE, NB, false>;
+    const int64_t blocks = need;
+    launch_k(c, kern, dim3((unsigned)blocks), dim3(warps * 32), a);
     return cudaGetLastError();
 }
 
