@@ -64,6 +64,39 @@ __global__ void __launch_bounds__(256, 4) swiglu_vec(const float4 *gate, const f
     }
 }
 
+// Non-persistent variant: CTA b owns units [b*256*U, (b+1)*256*U); thread t
+// handles units base + t + k*256 (k < U, coalesced per k), all 2*U loads
+// issued before any result is used.
+template <int U>
+__global__ void __launch_bounds__(256) swiglu_blk(const float4 *gate, const float4 *up, const float *row_w,
+                                                  float4 *out, uint32_t units, uint32_t cols4)
+{
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t base = blockIdx.x * (256u * U) + threadIdx.x;
+    float4 g[U], v[U];
+#pragma unroll
+    for (int k = 0; k < U; k++) {
+        const uint32_t u = base + 256u * k;
+        if (u < units) {
+            g[k] = ld_stream(gate + u);
+            v[k] = ld_stream(up + u);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < U; k++) {
+        const uint32_t u = base + 256u * k;
+        if (u >= units) break;
+        float4 o = make_float4(silu_mul(g[k].x, v[k].x), silu_mul(g[k].y, v[k].y), silu_mul(g[k].z, v[k].z),
+                               silu_mul(g[k].w, v[k].w));
+        if (row_w) {
+            const float w = __ldg(row_w + u / cols4);
+            o = make_float4(__fmul_rn(o.x, w), __fmul_rn(o.y, w), __fmul_rn(o.z, w), __fmul_rn(o.w, w));
+        }
+        out[u] = o;
+    }
+}
+
 __global__ void swiglu_scalar(const float *gate, const float *up, const float *row_w, float *out,
                               int64_t n, int64_t cols)
 {
@@ -220,6 +253,21 @@ cudaError_t launch_swiglu(const LaunchCtx &c, const float *gate, const float *up
         // One wave: at most as many CTAs as can be resident at once (a second
         // partial wave would double the latency at small sizes); each thread
         // then streams units with kSwigluUnroll x 2 loads in flight.
+        // Non-persistent blocks (measured, 4096 x 768: 7.9 us vs 9.7 us for the
+        // persistent grid-stride kernel; 32768 x 768: 46 us vs 56 us): one unit
+        // per thread up to ~2M units, two beyond.
+        if (units < ((int64_t)1 << 31)) {
+            auto *g4 = reinterpret_cast<const float4 *>(gate);
+            auto *u4 = reinterpret_cast<const float4 *>(up);
+            auto *o4 = reinterpret_cast<float4 *>(out);
+            const uint32_t uu = (uint32_t)units, c4 = (uint32_t)(cols / 4);
+            if (units <= ((int64_t)2 << 20))
+                launch_k(c, swiglu_blk<1>, dim3((uu + 255) / 256), dim3(256), g4, u4, row_w, o4, uu, c4);
+            else
+                launch_k(c, swiglu_blk<2>, dim3((uu + 511) / 512), dim3(256), g4, u4, row_w, o4, uu, c4);
+            return cudaGetLastError();
+        }
+        // Beyond 2^31 units: the persistent grid-stride kernel with 64-bit indices.
         const bool small = units < (int64_t)1 << 30;
         static int occ32 = 0, occ64 = 0;
         int &occ = small ? occ32 : occ64;
