@@ -158,6 +158,36 @@ __global__ void __launch_bounds__(128) combine_vec(const float4 *y, const int32_
     out[e] = f4_add(res, acc);
 }
 
+// Token-major expert outputs, 8 experts, 32-bit indices: the nine 128-bit
+// loads are volatile asm statements, so all are issued before the first is
+// consumed (the generic kernel lets the compiler interleave them with the
+// sum; measured at T=512: 7.3 vs 7.6-8.2 us).
+__global__ void __launch_bounds__(128) combine8_tokmajor(const float4 *y, const float *w, const float4 *residual,
+                                                         float4 *out, uint32_t n_tokens, uint32_t cols4)
+{
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n_tokens * cols4) return;
+    const uint32_t t = e / cols4, c = e - t * cols4;
+    float4 yv[8];
+    float wk[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) yv[k] = ld_stream_inflight(y + (t * 8 + k) * cols4 + c);
+    const float4 res = ld_stream_inflight(residual + e);
+#pragma unroll
+    for (int k = 0; k < 8; k++) wk[k] = __ldg(w + t * 8 + k);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        acc.x = __fadd_rn(acc.x, __fmul_rn(wk[k], yv[k].x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(wk[k], yv[k].y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(wk[k], yv[k].z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(wk[k], yv[k].w));
+    }
+    out[e] = f4_add(res, acc);
+}
+
 __global__ void combine_scalar(const float *y, const int32_t *y_rows, const float *w,
                                const float *residual, float *out, int64_t n_tokens, int n_used,
                                int64_t cols)
@@ -302,6 +332,11 @@ cudaError_t launch_combine(const LaunchCtx &c, const float *y, const int32_t *y_
         auto *y4 = reinterpret_cast<const float4 *>(y);
         auto *r4 = reinterpret_cast<const float4 *>(residual);
         auto *o4 = reinterpret_cast<float4 *>(out);
+        if (n_used == 8 && !y_rows && total * 8 < ((int64_t)1 << 31)) {
+            const uint32_t tt = (uint32_t)n_tokens, c4 = (uint32_t)cols4, tot = (uint32_t)total;
+            launch_k(c, combine8_tokmajor, dim3((tot + 127) / 128), dim3(128), y4, w, r4, o4, tt, c4);
+            return cudaGetLastError();
+        }
         if (n_used == 8)
             launch_k(c, combine_vec<8>, dim3(blocks), dim3(128), y4, y_rows, w, r4, o4, n_tokens, n_used, cols4);
         else
