@@ -303,6 +303,13 @@ void ds3_cuda_profile_enable(int on);
 /* Last error message of this thread's calls ("" if none). */
 const char *ds3_cuda_last_error(void);
 
+/* new: self-test of the bounded-wait path. Launches one kernel that waits on
+ * an mbarrier nothing will complete, giving up after `polls` polls, exactly
+ * as the TMA-staged kernels do when a copy never lands. Returns 0 when the
+ * wait ran out and was reported through the device error word (the word is
+ * consumed), -1 otherwise. No fault, trap or hang is involved. */
+int ds3_cuda_selftest_bounded_wait(uint32_t polls);
+
 /* Reads and clears the device error word (bit 0: bad token id; bit 1: a
  * bounded wait ran out). Synchronises the module stream. */
 uint32_t ds3_cuda_device_errors(void);

@@ -961,6 +961,21 @@ float ds3_cuda_timer_elapsed_ms(int a, int b)
     return ms;
 }
 
+int ds3_cuda_selftest_bounded_wait(uint32_t polls)
+{
+    if (!ready("selftest_bounded_wait") || G.capturing) return -1;
+    if (polls == 0 || polls > (1u << 20)) {
+        set_error("selftest_bounded_wait: polls must be in 1..2^20");
+        return -1;
+    }
+    cudaStreamSynchronize(G.stream);
+    take_device_errors();  // start from a clean word
+    if (ds3::launch_bounded_wait_selftest(ctx(), polls) != cudaSuccess) return -1;
+    if (cudaStreamSynchronize(G.stream) != cudaSuccess) return -1;
+    const uint32_t bits = take_device_errors();
+    return (bits & (1u << ds3::kErrWaitTimeout)) ? 0 : -1;
+}
+
 const char *ds3_cuda_last_error(void) { return g_last_error.c_str(); }
 
 uint32_t ds3_cuda_device_errors(void)

@@ -81,6 +81,8 @@ cudaError_t launch_moe_expert_lists(const LaunchCtx &c, const int32_t *idx, cons
                                     int32_t *ids, float *gscores, int32_t *slot_of, int64_t n_tokens, int n_used,
                                     int n_expert, int64_t cap);
 
+cudaError_t launch_bounded_wait_selftest(const LaunchCtx &c, uint32_t polls);
+
 cudaError_t launch_router_topk(const LaunchCtx &c, const float *logits, float *probs_out,
                                int32_t *idx, float *scores, int64_t n_tokens, int n_expert,
                                int n_used, int norm_topk);

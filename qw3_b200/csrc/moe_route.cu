@@ -89,7 +89,27 @@ __global__ void __launch_bounds__(kRouteThreads) moe_expert_lists_k(
     if (tid == 0) counts[ex] = (int32_t)base;
 }
 
+// Self-test of the bounded mbarrier wait: the barrier expects one arrival
+// that never comes; the wait must give up after `polls` polls and record the
+// timeout in the error word.
+__global__ void bounded_wait_selftest_k(uint32_t polls, unsigned *err)
+{
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_init_fence();
+    }
+    __syncwarp();
+    if (!mbar_wait(&bar, 0, polls) && threadIdx.x == 0) flag_error(err, kErrWaitTimeout);
+}
+
 }  // namespace
+
+cudaError_t launch_bounded_wait_selftest(const LaunchCtx &c, uint32_t polls)
+{
+    bounded_wait_selftest_k<<<1, 32, 0, c.stream>>>(polls, c.err);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_moe_expert_lists(const LaunchCtx &c, const int32_t *idx, const float *scores, int32_t *counts,
                                     int32_t *ids, float *gscores, int32_t *slot_of, int64_t n_tokens, int n_used,

@@ -84,6 +84,7 @@ _SIGS = {
     "profile_enable": (None, [_I]),
     "last_error": (C.c_char_p, []),
     "device_errors": (_U32, []),
+    "selftest_bounded_wait": (_I, [_U32]),
 }
 
 
@@ -368,3 +369,7 @@ def timer_elapsed_ms(a: int, b: int) -> float:
 
 def device_errors() -> int:
     return lib().ds3_cuda_device_errors()
+
+
+def selftest_bounded_wait(polls: int = 1000) -> int:
+    return lib().ds3_cuda_selftest_bounded_wait(polls)

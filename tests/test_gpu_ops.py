@@ -428,3 +428,17 @@ def test_argument_errors(ds3, B):
             ds3.buffer_view(x, 1024, 2048)  # past the end: NULL
     finally:
         v.free()
+
+
+def test_bounded_wait_gives_up_and_reports(ds3):
+    # A wait on an mbarrier nothing completes must return after its poll
+    # budget and raise the timeout bit, leaving the context usable.
+    assert ds3.selftest_bounded_wait(2000) == 0
+    assert ds3.device_errors() == 0
+    x = ds3.upload(I.normal(1, (2, 128)))
+    w = ds3.upload(I.gamma(128, 2))
+    try:
+        assert ds3.rms_norm(x, w, x, 128, 2, 1e-6) == 0  # context still healthy
+    finally:
+        x.free()
+        w.free()

@@ -76,3 +76,37 @@ def test_gloo_two_ranks_match_single_process(tmp_path, port):
                                   1e-6)
     assert np.array_equal(got["norm"], want_n)
     assert np.array_equal(got["q"], want_q)
+
+
+def _quitter(rank, world, port, out_path):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from qw3_b200.shard import gather_rows
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        return  # leaves between steps, without joining the gather
+    try:
+        gather_rows(torch.zeros((3, 4)), 6)
+        status = "completed"
+    except Exception as e:  # the survivor must see an error, not hang
+        status = "error: " + type(e).__name__
+    with open(out_path, "w") as f:
+        f.write(status)
+
+
+def test_rank_that_quits_makes_the_gather_fail_not_hang(tmp_path):
+    out = tmp_path / "status.txt"
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_quitter, args=(r, 2, port, str(out))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    assert all(p.exitcode is not None for p in procs), "a rank hung"
+    assert out.read_text().startswith("error"), out.read_text()
