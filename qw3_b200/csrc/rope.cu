@@ -282,8 +282,8 @@ __device__ __forceinline__ void head_from_smem(const __half *head, int j, float 
 // prefetched into registers, so the tile's cos/sin are ready when it lands.
 constexpr int kBulkWarps = 9;
 
-template <typename T, int TT, int NS>
-__global__ void __launch_bounds__(kBulkWarps * 32) qk_norm_rope_bulk(
+template <typename T, int TT, int NS, int W = kBulkWarps>
+__global__ void __launch_bounds__(W * 32) qk_norm_rope_bulk(
     const T *q_src, T *q_dst, const T *k_src, T *k_dst, const float *q_w, const float *k_w,
     const int32_t *pos, int64_t rows, int nq, int nk, const __grid_constant__ FreqTable ft, float eps,
     int do_norm, unsigned *err)
@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32) qk_norm_rope_bulk(
     __shared__ __align__(16) float wq[128];
     __shared__ __align__(16) float wk[128];
     __shared__ __align__(8) uint64_t bars[NS];
-    constexpr int kThreads = kBulkWarps * 32;
+    constexpr int kThreads = W * 32;
     constexpr int kPairSlots = (TT * 64 + kThreads - 1) / kThreads;
 
     const int tid = threadIdx.x;
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32) qk_norm_rope_bulk(
         const T *sk = sq + (size_t)TT * nq * 128;
         const int n_heads = tok * nh;
         const int n_groups = (n_heads + 3) >> 2;
-        for (int g = warp; g < n_groups; g += kBulkWarps) {
+        for (int g = warp; g < n_groups; g += W) {
             const int h = 4 * g + sub;
             const bool act = h < n_heads;
             const int hc = act ? h : 0;
@@ -425,7 +425,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32) qk_norm_rope_bulk(
     }
 }
 
-template <typename T, int TT, int NS>
+template <typename T, int TT, int NS, int W = kBulkWarps>
 cudaError_t run_bulk(const LaunchCtx &c, const void *qs, void *qd, const void *ks, void *kd, const float *q_w,
                      const float *k_w, const int32_t *pos, int64_t rows, int nq, int nk, const FreqTable &ft,
                      float eps, int do_norm)
@@ -433,17 +433,17 @@ cudaError_t run_bulk(const LaunchCtx &c, const void *qs, void *qd, const void *k
     const size_t smem = (size_t)NS * TT * (nq + nk) * 128 * sizeof(T);
     static size_t configured = 0;
     if (smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(qk_norm_rope_bulk<T, TT, NS>,
+        cudaError_t e = cudaFuncSetAttribute(qk_norm_rope_bulk<T, TT, NS, W>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         configured = smem;
     }
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_bulk<T, TT, NS>, kBulkWarps * 32, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_bulk<T, TT, NS, W>, W * 32, smem);
     if (per_sm < 1) per_sm = 1;
     const int64_t tiles = (rows + TT - 1) / TT;
     const int64_t cap = (int64_t)c.n_sm * per_sm;
-    launch_ks(c, qk_norm_rope_bulk<T, TT, NS>, dim3((unsigned)(tiles < cap ? tiles : cap)), dim3(kBulkWarps * 32),
+    launch_ks(c, qk_norm_rope_bulk<T, TT, NS, W>, dim3((unsigned)(tiles < cap ? tiles : cap)), dim3(W * 32),
               smem, (const T *)qs, (T *)qd, (const T *)ks, (T *)kd, q_w, k_w, pos, rows, nq, nk, ft, eps, do_norm,
               c.err);
     return cudaGetLastError();
@@ -559,12 +559,14 @@ cudaError_t launch_qk_norm_rope(const LaunchCtx &c, const void *q_src, void *q_d
     (void)wts;
     // fp16 storage at large token counts: the TMA-staged kernel (measured at
     // T=32768: 126 us vs 138 us for the register-tile kernel; fp32 is faster
-    // with the register-tile kernel, 176 us vs 203 us).
+    // with the register-tile kernel, 176 us vs 203 us). 2-token tiles, 3
+    // stages, 9 warps measured best against 18 or 12 warps and 4-token tiles.
     if (use_hd && storage && rows >= 2048) {
         const uintptr_t al = reinterpret_cast<uintptr_t>(q_src) | reinterpret_cast<uintptr_t>(k_src);
-        if ((al & 15u) == 0)
+        if ((al & 15u) == 0) {
             return run_bulk<__half, 2, 3>(c, q_src, q_dst, k_src, k_dst, q_w, k_w, pos, rows, nq, nk, ft, eps,
                                           do_norm);
+        }
     }
     if (storage)
         return run<__half>(c, q_src, q_dst, k_src, k_dst, q_w, k_w, pos, rows, nq, nk, hd, use_hd, ft, eps,
