@@ -104,6 +104,16 @@ int ds3_cuda_buffer_write(ds3_cuda_buffer_t *buf, size_t offset,
 int ds3_cuda_buffer_read (ds3_cuda_buffer_t *buf, size_t offset,
                           void *dst, size_t bytes);
 
+/* new: the same copies, enqueued on the module stream in order with the ops
+ * and not waited for (graph-capturable). The host memory must stay valid and
+ * unchanged until the stream is synchronised (ds3_cuda_synchronize or
+ * end_batch); page-locked host memory lets the copies run at full link rate
+ * without a staging copy. */
+int ds3_cuda_buffer_write_async(ds3_cuda_buffer_t *buf, size_t offset,
+                                const void *src, size_t bytes);
+int ds3_cuda_buffer_read_async (ds3_cuda_buffer_t *buf, size_t offset,
+                                void *dst, size_t bytes);
+
 /* ------------------------------------------------------------------ */
 /* Ops with a ds3_metal.h counterpart                                 */
 /* ------------------------------------------------------------------ */

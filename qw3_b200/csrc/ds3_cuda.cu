@@ -387,6 +387,36 @@ int ds3_cuda_buffer_read(ds3_cuda_buffer_t *buf, size_t offset, void *dst, size_
     return 0;
 }
 
+int ds3_cuda_buffer_write_async(ds3_cuda_buffer_t *buf, size_t offset, const void *src, size_t bytes)
+{
+    if (!ready("buffer_write_async")) return -1;
+    if (!buf || !src || offset + bytes > buf->bytes || buf->read_only) {
+        set_error("buffer_write_async: bad arguments");
+        return -1;
+    }
+    cudaError_t e = cudaMemcpyAsync((char *)dptr(buf) + offset, src, bytes, cudaMemcpyHostToDevice, G.stream);
+    if (e != cudaSuccess) {
+        set_error("buffer_write_async: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+int ds3_cuda_buffer_read_async(ds3_cuda_buffer_t *buf, size_t offset, void *dst, size_t bytes)
+{
+    if (!ready("buffer_read_async")) return -1;
+    if (!buf || !dst || offset + bytes > buf->bytes) {
+        set_error("buffer_read_async: bad arguments");
+        return -1;
+    }
+    cudaError_t e = cudaMemcpyAsync(dst, (char *)dptr(buf) + offset, bytes, cudaMemcpyDeviceToHost, G.stream);
+    if (e != cudaSuccess) {
+        set_error("buffer_read_async: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
 // ------------------------------------------------------- ops (Metal mirror)
 int ds3_cuda_rms_norm(const ds3_cuda_buffer_t *x, const ds3_cuda_buffer_t *weight, ds3_cuda_buffer_t *out,
                       uint32_t n, uint32_t n_rows, float eps)

@@ -48,6 +48,8 @@ _SIGS = {
     "buffer_size": (_SZ, [_P]),
     "buffer_write": (_I, [_P, _SZ, _P, _SZ]),
     "buffer_read": (_I, [_P, _SZ, _P, _SZ]),
+    "buffer_write_async": (_I, [_P, _SZ, _P, _SZ]),
+    "buffer_read_async": (_I, [_P, _SZ, _P, _SZ]),
     "rms_norm": (_I, [_P, _P, _P, _U32, _U32, _F]),
     "rope": (_I, [_P, _P, _P, _U32, _U32, _U32, _F]),
     "buffer_copy_f32": (_I, [_P, _P, _SZ]),
@@ -189,6 +191,18 @@ def buffer_write(buf: Buffer, offset: int, host: np.ndarray) -> int:
 def buffer_read(buf: Buffer, offset: int, host: np.ndarray) -> int:
     assert host.flags["C_CONTIGUOUS"]
     return lib().ds3_cuda_buffer_read(_h(buf), offset, host.ctypes.data, host.nbytes)
+
+
+def buffer_write_async(buf: Buffer, offset: int, host: np.ndarray) -> int:
+    """Enqueue a host->device copy; `host` must stay alive and unchanged until synchronize()."""
+    assert host.flags["C_CONTIGUOUS"]
+    return lib().ds3_cuda_buffer_write_async(_h(buf), offset, host.ctypes.data, host.nbytes)
+
+
+def buffer_read_async(buf: Buffer, offset: int, host: np.ndarray) -> int:
+    """Enqueue a device->host copy into `host`, valid after synchronize()."""
+    assert host.flags["C_CONTIGUOUS"]
+    return lib().ds3_cuda_buffer_read_async(_h(buf), offset, host.ctypes.data, host.nbytes)
 
 
 def upload(host: np.ndarray) -> Buffer:

@@ -442,3 +442,17 @@ def test_bounded_wait_gives_up_and_reports(ds3):
     finally:
         x.free()
         w.free()
+
+
+def test_async_copies_in_a_batch(ds3, B):
+    x = I.normal(3, (64, 2048))
+    w = I.gamma(2048, 4)
+    xb, wb, ob = B.empty(x.nbytes), B.up(w), B.empty(x.nbytes)
+    out = np.empty_like(x)
+    assert ds3.begin_batch() == 0
+    assert ds3.buffer_write_async(xb, 0, x) == 0
+    assert ds3.rms_norm(xb, wb, ob, 2048, 64, 1e-6) == 0
+    assert ds3.buffer_read_async(ob, 0, out) == 0
+    assert ds3.end_batch() == 0
+    assert_bitexact(out, f32(ob, ds3, x.shape), "async read")
+    assert ds3.buffer_write_async(xb, 8, x) == -1  # past the end
