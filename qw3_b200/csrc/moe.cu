@@ -298,22 +298,12 @@ cudaError_t launch_swiglu(const LaunchCtx &c, const float *gate, const float *up
             return cudaGetLastError();
         }
         // Beyond 2^31 units: the persistent grid-stride kernel with 64-bit indices.
-        const bool small = units < (int64_t)1 << 30;
-        static int occ32 = 0, occ64 = 0;
-        int &occ = small ? occ32 : occ64;
-        if (!occ && cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                        &occ, small ? (const void *)swiglu_vec<uint32_t> : (const void *)swiglu_vec<int64_t>, 256,
-                        0) != cudaSuccess)
+        static int occ = 0;
+        if (!occ && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, swiglu_vec<int64_t>, 256, 0) != cudaSuccess)
             occ = 4;
         const unsigned blocks = grid_for(c, (units + kSwigluUnits - 1) / kSwigluUnits, 256, occ > 0 ? occ : 4);
-        auto *g4 = reinterpret_cast<const float4 *>(gate);
-        auto *u4 = reinterpret_cast<const float4 *>(up);
-        auto *o4 = reinterpret_cast<float4 *>(out);
-        if (small)
-            launch_k(c, swiglu_vec<uint32_t>, dim3(blocks), dim3(256), g4, u4, row_w, o4, (uint32_t)units,
-                     (uint32_t)(cols / 4));
-        else
-            launch_k(c, swiglu_vec<int64_t>, dim3(blocks), dim3(256), g4, u4, row_w, o4, units, cols / 4);
+        launch_k(c, swiglu_vec<int64_t>, dim3(blocks), dim3(256), reinterpret_cast<const float4 *>(gate),
+                 reinterpret_cast<const float4 *>(up), row_w, reinterpret_cast<float4 *>(out), units, cols / 4);
     } else {
         launch_k(c, swiglu_scalar, dim3(grid_for(c, n, 256, 16)), dim3(256), gate, up, row_w, out, n, cols);
     }
