@@ -774,6 +774,15 @@ def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k):
     rec("moe_expert_lists_T512", 512, 512 * K * (4 + 4 + 4 + 4 + 4), time_launches(ds3, fn, 20, max_over_ranks, barrier),
         note="latency-bound permutation, one CTA per expert; bytes: idx, scores in; ids, scores, slot out")
 
+    # Next-row kernel: router projection (sequential fp32 dot products in the
+    # reference's order, CUDA cores) fused with softmax/top-8, 512 tokens.
+    xr_ = up(I.normal(5300, (512, H)))
+    wr_ = up(I.normal(5301, (E, H), 0.0, 0.05))
+    fn = [lambda: ds3.router_logits_topk(xr_, wr_, None, ixr, scr, 512, H, E, K, True)]
+    us_r = time_launches(ds3, fn, 20, max_over_ranks, barrier)
+    rec("router_logits_topk_T512", 512, 512 * (4 * H + 64) + E * H * 4, us_r,
+        note="bit-exact sequential fp32 projection: %.0f GFLOP/s on CUDA cores" % (2 * 512 * E * H / (us_r * 1e-3) / 1e9))
+
     # C2: decode batch of 64 tokens x 48 layers, one graph (per-layer inputs distinct).
     L, B2 = 48, 64
     hid = empty(L * B2 * H * 4)

@@ -267,6 +267,20 @@ int ds3_cuda_moe_expert_lists(const ds3_cuda_buffer_t *idx, const ds3_cuda_buffe
                               ds3_cuda_buffer_t *gscores, ds3_cuda_buffer_t *slot_of,
                               uint32_t n_tokens, uint32_t n_expert, uint32_t n_used, uint32_t cap);
 
+/* new: router projection + softmax + top-k + renorm in one call. Replaces
+ * ds3_metal_moe_ffn_router (ds3_metal.h:380-387) followed by
+ * moe_router_topk_batch_tokens. x fp32 [n_tokens, n_embd] (the ffn-normed
+ * hidden state); w_router fp32 [n_expert][n_embd] (GGUF layout, dequantized);
+ * logits_out fp32 [n_tokens, n_expert] or NULL (required unless n_expert is
+ * 128 and n_embd a multiple of 32); idx / scores as router_softmax_topk.
+ * Each logit is summed in the reference's order (from 0, ascending index,
+ * multiply then add), so logits and top-k indices are bit-exact. */
+int ds3_cuda_router_logits_topk(const ds3_cuda_buffer_t *x, const ds3_cuda_buffer_t *w_router,
+                                ds3_cuda_buffer_t *logits_out,
+                                ds3_cuda_buffer_t *idx, ds3_cuda_buffer_t *scores,
+                                uint32_t n_tokens, uint32_t n_embd, uint32_t n_expert, uint32_t n_used,
+                                bool norm_topk_prob);
+
 /* SwiGLU with optional per-row routing weight:
  * out[r][c] = (silu(gate[r][c]) * up[r][c]) * row_weight[r]. row_weight may be
  * NULL (plain silu_mul, metal/moe.metal:95-108). */

@@ -38,6 +38,7 @@ _SIGS = {
     "swiglu": (None, [_P, _P, _P, _P, _I64, _I64, _I]),
     "moe_combine_residual": (None, [_P, _P, _P, _P, _P, _I64, _I, _I64, _I]),
     "max_threads": (_I, []),
+    "router_logits": (None, [_P, _P, _I64, _I, _I, _P, _I]),
 }
 _PORT_ONLY = {
     "dequant_row": (_I, [_I, _P, _I64, _P]),
@@ -155,6 +156,15 @@ class Oracle:
         sc = np.empty((T, n_used), np.float32)
         self._router_softmax_topk(_p(logits), T, E, n_used, 1 if norm else 0, _p(probs), _p(idx), _p(sc), nthreads)
         return probs, idx, sc
+
+    def router_logits(self, x, W, nthreads=1):
+        """x [T, n_embd], W [n_expert, n_embd] -> logits [T, n_expert]."""
+        x, W = _arr(x, np.float32), _arr(W, np.float32)
+        T, K = x.shape
+        E = W.shape[0]
+        out = np.empty((T, E), np.float32)
+        self._router_logits(_p(x), _p(W), T, K, E, _p(out), nthreads)
+        return out
 
     # ----------------------------------------------------------------- moe
     def swiglu(self, gate, up, row_w=None, nthreads=1):

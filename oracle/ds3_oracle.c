@@ -454,3 +454,19 @@ int ds3o_moe_expert_lists(const int32_t *idx, const float *scores, int64_t n_tok
     }
     return rc;
 }
+
+/* Vector x matrix as ds3_ref_vec_matmul, src/ds3_reference.c:424-434. */
+void ds3o_router_logits(const float *x, const float *W, int64_t n_tokens, int n_embd, int n_expert,
+                        float *logits, int nthreads)
+{
+#pragma omp parallel for num_threads(clamp_threads(nthreads)) schedule(static)
+    for (int64_t t = 0; t < n_tokens; t++) {
+        const float *xr = x + t * n_embd;
+        for (int e = 0; e < n_expert; e++) {
+            const float *wr = W + (int64_t)e * n_embd;
+            float acc = 0.0f;
+            for (int i = 0; i < n_embd; i++) acc += xr[i] * wr[i];
+            logits[t * n_expert + e] = acc;
+        }
+    }
+}

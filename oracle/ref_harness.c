@@ -183,3 +183,11 @@ void ds3r_moe_combine_residual(const float *y, const int32_t *y_rows, const floa
         free(acc);
     }
 }
+
+void ds3r_router_logits(const float *x, const float *W, int64_t n_tokens, int n_embd, int n_expert,
+                        float *logits, int nthreads)
+{
+#pragma omp parallel for num_threads(nt(nthreads)) schedule(static)
+    for (int64_t t = 0; t < n_tokens; t++)
+        ds3_ref_vec_matmul(x + t * n_embd, W, logits + t * n_expert, n_embd, n_expert);
+}

@@ -19,7 +19,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libds3cuda.so"
-SOURCES = ["ds3_cuda.cu", "norm.cu", "embed.cu", "rope.cu", "router.cu", "moe.cu", "moe_route.cu"]
+SOURCES = ["ds3_cuda.cu", "norm.cu", "embed.cu", "rope.cu", "router.cu", "moe.cu", "moe_route.cu", "router_gemv.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -832,6 +832,37 @@ int ds3_cuda_router_softmax_topk(const ds3_cuda_buffer_t *logits, ds3_cuda_buffe
                          norm_topk_prob);
 }
 
+int ds3_cuda_router_logits_topk(const ds3_cuda_buffer_t *x, const ds3_cuda_buffer_t *w_router,
+                                ds3_cuda_buffer_t *logits_out, ds3_cuda_buffer_t *idx, ds3_cuda_buffer_t *scores,
+                                uint32_t n_tokens, uint32_t n_embd, uint32_t n_expert, uint32_t n_used,
+                                bool norm_topk_prob)
+{
+    const char *op = "router_logits_topk";
+    if (!ready(op)) return -1;
+    if (n_embd == 0 || n_expert == 0 || n_used == 0 || n_used > n_expert || n_used > 64) {
+        set_error("%s: need n_embd > 0 and 0 < n_used <= min(n_expert, 64)", op);
+        return -1;
+    }
+    const size_t ob = (size_t)n_tokens * n_used * 4;
+    if (!need(op, "x", x, (size_t)n_tokens * n_embd * 4) || !need(op, "w_router", w_router, (size_t)n_expert * n_embd * 4) ||
+        !need(op, "idx", idx, ob) || !writable(op, "idx", idx) || !need(op, "scores", scores, ob) ||
+        !writable(op, "scores", scores) ||
+        (logits_out && (!need(op, "logits_out", logits_out, (size_t)n_tokens * n_expert * 4) ||
+                        !writable(op, "logits_out", logits_out))))
+        return -1;
+    if (!logits_out && !ds3::router_gemv_fast(n_tokens, (int)n_embd, (int)n_expert, (int)n_used, dptr(x), dptr(w_router))) {
+        set_error("%s: logits_out is required for this shape (fast path: n_expert 128, n_embd %% 32 == 0)", op);
+        return -1;
+    }
+    ProfScope ps(op);
+    return finish(op,
+                  ds3::launch_router_gemv_topk(ctx(), (const float *)dptr(x), (const float *)dptr(w_router),
+                                               (float *)dptr(logits_out), (int32_t *)dptr(idx), (float *)dptr(scores),
+                                               n_tokens, (int)n_embd, (int)n_expert, (int)n_used,
+                                               norm_topk_prob ? 1 : 0),
+                  ps);
+}
+
 int ds3_cuda_moe_expert_lists(const ds3_cuda_buffer_t *idx, const ds3_cuda_buffer_t *scores, ds3_cuda_buffer_t *counts,
                               ds3_cuda_buffer_t *ids, ds3_cuda_buffer_t *gscores, ds3_cuda_buffer_t *slot_of,
                               uint32_t n_tokens, uint32_t n_expert, uint32_t n_used, uint32_t cap)

@@ -83,6 +83,12 @@ cudaError_t launch_moe_expert_lists(const LaunchCtx &c, const int32_t *idx, cons
 
 cudaError_t launch_bounded_wait_selftest(const LaunchCtx &c, uint32_t polls);
 
+// Router projection (sequential fp32 dot products, reference order) + top-k.
+bool router_gemv_fast(int64_t n_tokens, int n_embd, int n_expert, int n_used, const void *x, const void *W);
+cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const float *W, float *logits_out,
+                                    int32_t *idx, float *scores, int64_t n_tokens, int n_embd, int n_expert,
+                                    int n_used, int norm_topk);
+
 cudaError_t launch_router_topk(const LaunchCtx &c, const float *logits, float *probs_out,
                                int32_t *idx, float *scores, int64_t n_tokens, int n_expert,
                                int n_used, int norm_topk);

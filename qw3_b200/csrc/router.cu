@@ -19,16 +19,10 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "router_select.cuh"
 
 namespace ds3 {
 namespace {
-
-// Monotone map of a (non-NaN) float onto unsigned integers.
-__device__ __forceinline__ unsigned order_key(float x)
-{
-    const unsigned u = __float_as_uint(x);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi)
 {
@@ -62,75 +56,8 @@ __global__ void __launch_bounds__(128) router_warp(const float *logits, float *p
         for (int j = 0; j < V; j++) x[j] = __ldcs(row + lane * V + j);
     }
 
-    float mx = x[0];
-#pragma unroll
-    for (int j = 1; j < V; j++) mx = fmaxf(mx, x[j]);
-    mx = warp_max(mx);
-    float p[V];
-    float part = 0.0f;
-#pragma unroll
-    for (int j = 0; j < V; j++) {
-        p[j] = expf(__fsub_rn(x[j], mx));
-        part = __fadd_rn(part, p[j]);
-    }
-    const float total = warp_sum(part);
-    const float inv = __fdiv_rn(1.0f, total);
-#pragma unroll
-    for (int j = 0; j < V; j++) p[j] = __fmul_rn(p[j], inv);
-
-    if (probs_out) {
-        float *po = probs_out + t * E + lane * V;
-        if constexpr (V % 4 == 0) {
-#pragma unroll
-            for (int j = 0; j < V; j += 4)
-                *reinterpret_cast<float4 *>(po + j) = make_float4(p[j], p[j + 1], p[j + 2], p[j + 3]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < V; j++) po[j] = p[j];
-        }
-    }
-
-    // Selection keys: the float order of the logits as unsigned integers, so a
-    // round is a local scan plus one redux.sync max and one ballot (lowest
-    // lane = lowest expert index among equal logits; -0 is folded into +0).
-    unsigned key[V];
-#pragma unroll
-    for (int j = 0; j < V; j++) key[j] = order_key(__fadd_rn(x[j], 0.0f));
-    unsigned used = 0;
-    int my_idx = -1;
-    float my_sc = 0.0f;
-    float sum_sel = 0.0f;
-    for (int k = 0; k < n_used; k++) {
-        unsigned best = 0;
-        int bj = -1;
-#pragma unroll
-        for (int j = 0; j < V; j++)
-            if (!((used >> j) & 1u) && key[j] > best) {
-                best = key[j];
-                bj = j;
-            }
-        const unsigned m = __reduce_max_sync(kFull, best);
-        const unsigned ball = __ballot_sync(kFull, bj >= 0 && best == m);
-        if (ball == 0) break;  // fewer experts than n_used (host rejects this)
-        const int owner = __ffs(ball) - 1;
-        const int sel = __shfl_sync(kFull, bj, owner);
-        float pj = p[0];
-#pragma unroll
-        for (int j = 1; j < V; j++)
-            if (j == sel) pj = p[j];
-        if (lane == owner) used |= 1u << sel;
-        const float sc = __shfl_sync(kFull, pj, owner);
-        sum_sel = __fadd_rn(sum_sel, sc);
-        if (lane == k) {
-            my_idx = owner * V + sel;
-            my_sc = sc;
-        }
-    }
-    if (norm_topk && sum_sel > 0.0f) my_sc = __fmul_rn(my_sc, __fdiv_rn(1.0f, sum_sel));
-    if (lane < n_used) {
-        idx[t * n_used + lane] = my_idx;
-        scores[t * n_used + lane] = my_sc;
-    }
+    router_select<V>(x, lane, n_used, norm_topk, probs_out ? probs_out + t * E : nullptr, idx + t * n_used,
+                     scores + t * n_used);
 }
 
 // Any n_expert / n_used (used when the warp layout does not fit): one thread

@@ -74,6 +74,7 @@ _SIGS = {
     "qk_norm_rope_kv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _F, _F, _I]),
     "kv_cache_write_batch": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32]),
     "swiglu": (_I, [_P, _P, _P, _P, _U32, _U32]),
+    "router_logits_topk": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _B]),
     "moe_expert_lists": (_I, [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32]),
     "moe_combine_residual": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32]),
     "stream": (_P, []),
@@ -333,6 +334,12 @@ def kv_cache_write_batch(k, v, k_cache, v_cache, seq_pos, n_tokens, max_seq_len,
 def router_softmax_topk(logits, probs_out, idx, scores, n_tokens, n_expert, n_used, norm_topk_prob) -> int:
     return lib().ds3_cuda_router_softmax_topk(_h(logits), _h(probs_out), _h(idx), _h(scores), n_tokens,
                                               n_expert, n_used, bool(norm_topk_prob))
+
+
+def router_logits_topk(x, w_router, logits_out, idx, scores, n_tokens, n_embd, n_expert, n_used,
+                       norm_topk_prob=True) -> int:
+    return lib().ds3_cuda_router_logits_topk(_h(x), _h(w_router), _h(logits_out), _h(idx), _h(scores), n_tokens,
+                                             n_embd, n_expert, n_used, bool(norm_topk_prob))
 
 
 def moe_expert_lists(idx, scores, counts, ids, gscores, slot_of, n_tokens, n_expert, n_used, cap) -> int:

@@ -290,3 +290,10 @@ def test_moe_expert_lists_engine_layout(port):
     assert list(slot) == [6, 0, 1, 3, 7, 4]
     rc, *_ = oracle.moe_expert_lists(port, np.array([[5, 0]], np.int32), sc[:1], 3, 3)
     assert rc == -1
+
+
+@needs_ref
+def test_router_logits_equal_reference_vec_matmul(port):
+    x = I.normal(40, (9, 2048))
+    W = I.normal(41, (128, 2048), 0.0, 0.05)
+    assert_bitexact(port.router_logits(x, W), ref.router_logits(x, W))
