@@ -272,7 +272,7 @@ int ds3_cuda_moe_expert_lists(const ds3_cuda_buffer_t *idx, const ds3_cuda_buffe
  * moe_router_topk_batch_tokens. x fp32 [n_tokens, n_embd] (the ffn-normed
  * hidden state); w_router fp32 [n_expert][n_embd] (GGUF layout, dequantized);
  * logits_out fp32 [n_tokens, n_expert] or NULL (required unless n_expert is
- * 128 and n_embd a multiple of 32); idx / scores as router_softmax_topk.
+ * 128 and n_embd a multiple of 64); idx / scores as router_softmax_topk.
  * Each logit is summed in the reference's order (from 0, ascending index,
  * multiply then add), so logits and top-k indices are bit-exact. */
 int ds3_cuda_router_logits_topk(const ds3_cuda_buffer_t *x, const ds3_cuda_buffer_t *w_router,

@@ -851,7 +851,7 @@ int ds3_cuda_router_logits_topk(const ds3_cuda_buffer_t *x, const ds3_cuda_buffe
                         !writable(op, "logits_out", logits_out))))
         return -1;
     if (!logits_out && !ds3::router_gemv_fast(n_tokens, (int)n_embd, (int)n_expert, (int)n_used, dptr(x), dptr(w_router))) {
-        set_error("%s: logits_out is required for this shape (fast path: n_expert 128, n_embd %% 32 == 0)", op);
+        set_error("%s: logits_out is required for this shape (fast path: n_expert 128, n_embd %% 64 == 0)", op);
         return -1;
     }
     ProfScope ps(op);

@@ -9,17 +9,29 @@
 //
 // The top-8 indices must match the reference exactly, which the logits do
 // only if every dot product is accumulated in the reference's order. So the
-// projection runs on the CUDA cores, one thread per (token, expert), each
-// summing its 2048 products sequentially with separately rounded multiply
-// and add (no FMA) - a tensor-core or tree-reduced dot product would round
-// differently. A CTA owns 4 tokens x 128 experts, one expert per thread,
-// with 4 independent sums per thread (one per token). W (GGUF layout
-// [n_expert][n_embd]) is loaded 32 columns at a time with coalesced 128-bit
-// loads (the next chunk prefetched into registers while the current one is
-// consumed) and stored transposed in shared memory, so a warp's 32 experts
-// read 32 consecutive words; each W word read serves 4 multiply-adds and the
-// token columns come as 128-bit broadcast reads covering 4 columns. The logits then go through the same
-// warp-level selection as router_softmax_topk (router_select.cuh).
+// projection runs on the CUDA cores, one sum per (token, expert), each adding
+// its 2048 products sequentially with separately rounded multiply and add (no
+// FMA) - a tensor-core or tree-reduced dot product would round differently.
+// Products are formed two at a time with the packed fp32 multiply of sm_100
+// (mul.rn.f32x2, two independent IEEE products); the adds stay scalar and in
+// order.
+//
+// Work split (fast path: 128 experts, n_embd % 64 == 0). A cluster of 4 CTAs
+// shares up to 16 tokens and CTA r owns experts 32r .. 32r+31, so each CTA
+// reads a quarter of W (GGUF layout [n_expert][n_embd]). Four compute warps
+// hold lane = expert, 4 tokens each; four copy warps stream the CTA's 32 W
+// rows and the cluster's token rows, 64 columns at a time, into a 6-stage
+// ring in shared memory with 16-byte cp.async copies that complete on
+// per-stage mbarriers (a copy warp arrives once its own copies have landed).
+// Rows sit at a stride of 68 floats, so the 128-bit reads of 8 lanes (8
+// different W rows) hit 32 distinct banks; token columns are broadcast reads.
+// Each CTA asks for more than half an SM's shared memory, so the hardware
+// places one CTA per SM, and the host sizes tokens per cluster from the number
+// of clusters that can be resident at once, so one wave covers the tokens.
+// When the sums are done, warp w stores its logits into the shared memory of
+// CTA w (distributed shared memory), and after a cluster barrier CTA r runs
+// the warp-level selection of router_softmax_topk (router_select.cuh) for
+// tokens 4r .. 4r+3 of the cluster.
 #include "common.cuh"
 #include "launch.h"
 #include "router_select.cuh"
@@ -27,85 +39,243 @@
 namespace ds3 {
 namespace {
 
-constexpr int kRgE = 128;                  // experts (fast path): 4 warps x 32 lanes
-constexpr int kRgTok = 4;                  // tokens per CTA, one accumulator each per lane
-constexpr int kRgKC = 32;                  // columns per chunk
-constexpr int kRgThreads = kRgE;           // 128
+constexpr int kRgE = 128;                    // experts on the fast path
 
-__global__ void __launch_bounds__(kRgThreads) router_gemv_topk_k(const float *x, const float *W, float *logits_out,
-                                                                 int32_t *idx, float *scores, int64_t n_tokens,
-                                                                 int n_embd, int n_used, int norm_topk)
+constexpr int kClKC = 64;                    // columns per stage
+constexpr int kClLd = kClKC + 4;             // padded row stride (floats), 16-byte multiple
+constexpr int kClStages = 6;
+constexpr int kClPW = 4;                     // copy warps
+constexpr int kClSeg = kClKC / 4;            // 16-byte segments per row and stage
+constexpr size_t kClMinSmem = 116 * 1024;    // > half an SM's shared memory: one CTA per SM
+
+// CN CTAs per cluster, NW compute warps with TPW tokens each, PW copy warps.
+// The launcher uses <4, 4, 4, 4>; at 512 tokens, 8x2 compute warps and 8 or
+// 12 copy warps measured the same or slower, and 1 or 2 copy warps or 2-CTA
+// clusters clearly slower.
+template <int CN, int NW, int TPW, int PW = kClPW>
+struct ClLayout {
+    static constexpr int kEpC = kRgE / CN;                            // experts per CTA
+    static constexpr int kEpL = kEpC / 32;                            // experts per lane
+    static constexpr int kThreads = 32 * (NW + PW);
+    static constexpr int kTok = NW * TPW;                             // max tokens per cluster
+    static constexpr int kSel = kTok / CN;                            // tokens each CTA selects for
+    static constexpr int kStageFloats = (kEpC + kTok) * kClLd;
+    static constexpr size_t kSmemUsed = (size_t)kClStages * kStageFloats * 4 + (size_t)kSel * kRgE * 4;
+    static constexpr size_t kSmem = kSmemUsed > kClMinSmem ? kSmemUsed : kClMinSmem;
+    static_assert(kTok <= 32 && kTok % CN == 0 && kSel <= NW + PW && kEpC % 32 == 0, "layout");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank()
 {
-    __shared__ float ws[kRgKC][kRgE + 1];  // chunk of W, transposed; +1 keeps the transposing stores conflict-free
-    __shared__ __align__(16) float xs[kRgTok][kRgKC];
-    __shared__ __align__(16) float lg[kRgTok][kRgE];
-    pdl_wait();
-    pdl_trigger();
-    const int e = threadIdx.x;  // expert owned by this thread
-    const int64_t t0 = (int64_t)blockIdx.x * kRgTok;
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+// Store one float into the shared memory of CTA `rank` of this cluster, at the
+// offset `local` has in this CTA.
+__device__ __forceinline__ void st_cluster_f32(const float *local, uint32_t rank, float v)
+{
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(local)), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+// Arrive on `bar` once this thread's earlier cp.async copies have landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar)
+{
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// Two independent round-to-nearest fp32 products in one packed instruction
+// (sm_100): {a.x * b.x, a.y * b.y}, each rounded exactly as __fmul_rn.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b)
+{
+    unsigned long long ra, rb, rd;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+    float2 d;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
+    return d;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
 
-    // Coalesced staging: float4 q = e + h*128 of the 128 x 32 chunk is row
-    // q / 8, columns 4 * (q % 8) .. +3 (8 threads read 128 contiguous bytes).
-    constexpr int kH = kRgE * kRgKC / 4 / kRgThreads;  // 8
-    float4 w[kH];
-    float xr = 0.0f;
-    auto fetch = [&](int k0) {
-#pragma unroll
-        for (int h = 0; h < kH; h++) {
-            const int q = e + h * kRgThreads;
-            w[h] = __ldg(reinterpret_cast<const float4 *>(W + (int64_t)(q / 8) * n_embd + k0 + 4 * (q % 8)));
+// tpc = tokens per cluster (<= NW * TPW), chosen by the host so that the
+// clusters fill the GPU in one wave.
+template <int CN, int NW, int TPW, int PW>
+__global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW>::kThreads, 1)
+    router_gemv_cluster_k(const float *x, const float *W, float *logits_out, int32_t *idx, float *scores,
+                          int64_t n_tokens, int n_embd, int n_used, int norm_topk, int tpc, unsigned *err)
+{
+    using L = ClLayout<CN, NW, TPW, PW>;
+    extern __shared__ __align__(16) float sm[];
+    float *lgx = sm + kClStages * L::kStageFloats;  // [kSel][128] logits of the tokens this CTA selects for
+    __shared__ __align__(8) uint64_t full[kClStages], empty[kClStages];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int64_t t0 = (int64_t)(blockIdx.x / CN) * tpc;
+    const int nt = n_tokens - t0 < tpc ? (int)(n_tokens - t0) : tpc;
+    const int e0 = (int)rank * L::kEpC;
+    const int n_chunks = n_embd / kClKC;  // n_embd % kClKC == 0 on this path
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kClStages; s++) {
+            mbar_init(&full[s], 32 * PW);
+            mbar_init(&empty[s], NW);
         }
-        const int64_t tt = t0 + e / kRgKC;  // 128 threads stage 4 tokens x 32 columns
-        xr = tt < n_tokens ? x[tt * n_embd + k0 + e % kRgKC] : 0.0f;
-    };
-    fetch(0);
-    float acc[kRgTok];
-#pragma unroll
-    for (int j = 0; j < kRgTok; j++) acc[j] = 0.0f;
-    for (int k0 = 0; k0 < n_embd; k0 += kRgKC) {
-#pragma unroll
-        for (int h = 0; h < kH; h++) {
-            const int q = e + h * kRgThreads;
-            const int r = q / 8, c = 4 * (q % 8);
-            ws[c][r] = w[h].x;
-            ws[c + 1][r] = w[h].y;
-            ws[c + 2][r] = w[h].z;
-            ws[c + 3][r] = w[h].w;
-        }
-        xs[e / kRgKC][e % kRgKC] = xr;
-        __syncthreads();
-        if (k0 + kRgKC < n_embd) fetch(k0 + kRgKC);  // next chunk in flight during the sums
-#pragma unroll
-        for (int i = 0; i < kRgKC / 4; i++) {
-            float xv[kRgTok][4];
-#pragma unroll
-            for (int j = 0; j < kRgTok; j++) {
-                const float4 v = *reinterpret_cast<const float4 *>(&xs[j][4 * i]);
-                xv[j][0] = v.x; xv[j][1] = v.y; xv[j][2] = v.z; xv[j][3] = v.w;
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const float wv = ws[4 * i + u][e];
-#pragma unroll
-                for (int j = 0; j < kRgTok; j++) acc[j] = __fadd_rn(acc[j], __fmul_rn(xv[j][u], wv));
-            }
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int j = 0; j < kRgTok; j++) {
-        lg[j][e] = acc[j];
-        if (logits_out && t0 + j < n_tokens) logits_out[(t0 + j) * kRgE + e] = acc[j];
+        mbar_init_fence();
     }
     __syncthreads();
+    cluster_arrive_relaxed();  // every CTA of the cluster has started (waited on before the logit exchange)
+    pdl_wait();
+    pdl_trigger();
 
-    const int warp = e >> 5, lane = e & 31;
-    if (t0 + warp < n_tokens) {  // warp w selects for token t0 + w
-        const float4 v = *reinterpret_cast<const float4 *>(&lg[warp][4 * lane]);
-        const float xv[4] = {v.x, v.y, v.z, v.w};
-        const int64_t tw = t0 + warp;
-        router_select<4>(xv, lane, n_used, norm_topk, nullptr, idx + tw * n_used, scores + tw * n_used);
+    bool ok = true;
+    float acc[L::kEpL][TPW];
+#pragma unroll
+    for (int m = 0; m < L::kEpL; m++)
+#pragma unroll
+        for (int j = 0; j < TPW; j++) acc[m][j] = 0.0f;
+    if (warp >= NW) {
+        // Copy warps: 16-byte async copies of the kEpC W rows and nt token
+        // rows of each stage; every copy thread arrives on full[s] once its
+        // own copies have landed.
+        const int pt = threadIdx.x - 32 * NW;
+        for (int c = 0; c < n_chunks; c++) {
+            const int s = c % kClStages;
+            if (c >= kClStages && !mbar_wait(&empty[s], ((c / kClStages) - 1) & 1, kWaitLimit)) {
+                ok = false;
+                break;
+            }
+            const int k0 = c * kClKC;
+            float *st = sm + s * L::kStageFloats;
+            for (int q = pt; q < (L::kEpC + L::kTok) * kClSeg; q += 32 * PW) {
+                const int row = q / kClSeg, seg = q % kClSeg;
+                if (row < L::kEpC)
+                    cp_async16(st + row * kClLd + 4 * seg, W + (int64_t)(e0 + row) * n_embd + k0 + 4 * seg);
+                else if (row - L::kEpC < nt)
+                    cp_async16(st + row * kClLd + 4 * seg, x + (t0 + row - L::kEpC) * n_embd + k0 + 4 * seg);
+            }
+            cp_async_arrive(&full[s]);
+        }
+        // Do not leave with copies in flight.
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else {
+        for (int c = 0; c < n_chunks; c++) {
+            const int s = c % kClStages;
+            if (!mbar_wait(&full[s], (c / kClStages) & 1, kWaitLimit)) {
+                ok = false;
+                break;
+            }
+            const float *st = sm + s * L::kStageFloats;
+            const float *xr = st + (L::kEpC + warp * TPW) * kClLd;
+#pragma unroll
+            for (int i = 0; i < kClKC / 4; i++) {
+                float wv[L::kEpL][4];
+#pragma unroll
+                for (int m = 0; m < L::kEpL; m++) {
+                    const float4 w4 = *reinterpret_cast<const float4 *>(st + (lane + 32 * m) * kClLd + 4 * i);
+                    wv[m][0] = w4.x; wv[m][1] = w4.y; wv[m][2] = w4.z; wv[m][3] = w4.w;
+                }
+                // Products of columns (k, k+1) and (k+2, k+3) two at a time for
+                // every sum, then the four sequential adds, round-robin over the
+                // independent sums so consecutive adds do not wait on each other.
+                float pr[L::kEpL][TPW][4];
+#pragma unroll
+                for (int j = 0; j < TPW; j++) {
+                    const float4 v = *reinterpret_cast<const float4 *>(xr + j * kClLd + 4 * i);
+#pragma unroll
+                    for (int m = 0; m < L::kEpL; m++) {
+                        const float2 p01 = mul2_rn(make_float2(v.x, v.y), make_float2(wv[m][0], wv[m][1]));
+                        const float2 p23 = mul2_rn(make_float2(v.z, v.w), make_float2(wv[m][2], wv[m][3]));
+                        pr[m][j][0] = p01.x; pr[m][j][1] = p01.y; pr[m][j][2] = p23.x; pr[m][j][3] = p23.y;
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+#pragma unroll
+                    for (int j = 0; j < TPW; j++)
+#pragma unroll
+                        for (int m = 0; m < L::kEpL; m++) acc[m][j] = __fadd_rn(acc[m][j], pr[m][j][u]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
     }
+    if (!ok) flag_error(err, kErrWaitTimeout);
+
+    cluster_wait_acquire();  // all CTAs resident before the remote stores
+    if (warp < NW) {
+#pragma unroll
+        for (int j = 0; j < TPW; j++) {
+            const int tl = warp * TPW + j;
+            if (tl < nt) {
+#pragma unroll
+                for (int m = 0; m < L::kEpL; m++) {
+                    const int e = e0 + lane + 32 * m;
+                    if (logits_out) logits_out[(t0 + tl) * kRgE + e] = acc[m][j];
+                    st_cluster_f32(lgx + (tl % L::kSel) * kRgE + e, (uint32_t)(tl / L::kSel), acc[m][j]);
+                }
+            }
+        }
+    }
+    cluster_arrive_release();
+    cluster_wait_acquire();
+    if (warp < L::kSel) {
+        const int tl = (int)rank * L::kSel + warp;  // this CTA selects for tokens kSel*rank ..
+        if (tl < nt) {
+            const float4 v = *reinterpret_cast<const float4 *>(lgx + warp * kRgE + 4 * lane);
+            const float xv[4] = {v.x, v.y, v.z, v.w};
+            const int64_t tw = t0 + tl;
+            router_select<4>(xv, lane, n_used, norm_topk, nullptr, idx + tw * n_used, scores + tw * n_used);
+        }
+    }
+}
+
+template <int CN, int NW, int TPW, int PW = kClPW>
+cudaError_t launch_cluster(const LaunchCtx &c, const float *x, const float *W, float *logits_out, int32_t *idx,
+                           float *scores, int64_t n_tokens, int n_embd, int n_used, int norm_topk)
+{
+    using L = ClLayout<CN, NW, TPW, PW>;
+    auto kern = router_gemv_cluster_k<CN, NW, TPW, PW>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(L::kThreads);
+    cfg.dynamicSmemBytes = L::kSmem;
+    cfg.stream = c.stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CN;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    static int max_clusters = 0;  // clusters resident at once, queried once per process
+    if (max_clusters == 0) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kSmem);
+        if (e != cudaSuccess) return e;
+        cfg.gridDim = dim3(CN);
+        cfg.numAttrs = 1;
+        e = cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg);
+        if (e != cudaSuccess) return e;
+        if (max_clusters < 1) max_clusters = 1;
+    }
+    // Fewest tokens per cluster that still lets one wave of clusters cover n_tokens.
+    int64_t tpc = (n_tokens + max_clusters - 1) / max_clusters;
+    if (tpc > L::kTok) tpc = L::kTok;
+    if (tpc < 1) tpc = 1;
+    cfg.gridDim = dim3((unsigned)(((n_tokens + tpc - 1) / tpc) * CN));
+    cfg.numAttrs = c.pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk,
+                              (int)tpc, c.err);
 }
 
 // Any shape: one thread per (token, expert) straight from global memory, same
@@ -130,7 +300,7 @@ __global__ void router_logits_k(const float *x, const float *W, float *logits, i
 bool router_gemv_fast(int64_t n_tokens, int n_embd, int n_expert, int n_used, const void *x, const void *W)
 {
     const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(W);
-    return n_expert == kRgE && n_embd % kRgKC == 0 && n_used <= 32 && (al & 15u) == 0 && n_tokens > 0;
+    return n_expert == kRgE && n_embd % kClKC == 0 && n_used <= 32 && (al & 15u) == 0 && n_tokens > 0;
 }
 
 cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const float *W, float *logits_out,
@@ -138,11 +308,8 @@ cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const fl
                                     int n_used, int norm_topk)
 {
     if (n_tokens <= 0) return cudaSuccess;
-    if (router_gemv_fast(n_tokens, n_embd, n_expert, n_used, x, W)) {
-        launch_k(c, router_gemv_topk_k, dim3((unsigned)((n_tokens + kRgTok - 1) / kRgTok)), dim3(kRgThreads), x, W,
-                 logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk);
-        return cudaGetLastError();
-    }
+    if (router_gemv_fast(n_tokens, n_embd, n_expert, n_used, x, W))
+        return launch_cluster<4, 4, 4, 4>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk);
     if (!logits_out) return cudaErrorInvalidValue;  // the general path needs the logits buffer
     const int64_t n = n_tokens * n_expert;
     launch_k(c, router_logits_k, dim3((unsigned)((n + 255) / 256)), dim3(256), x, W, logits_out, n_tokens, n_embd,

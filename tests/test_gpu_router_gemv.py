@@ -30,7 +30,8 @@ def up(ds3):
 
 @pytest.mark.parametrize("T,K,E,n_used,with_logits", [(512, 2048, 128, 8, True), (512, 2048, 128, 8, False),
                                                       (1, 2048, 128, 8, True), (67, 1024, 128, 8, True),
-                                                      (13, 100, 64, 4, True), (5, 2048, 32, 8, True)])
+                                                      (13, 100, 64, 4, True), (5, 2048, 32, 8, True),
+                                                      (70, 2080, 128, 8, True), (1000, 2048, 128, 8, True)])
 def test_router_logits_topk(ds3, up, port, T, K, E, n_used, with_logits):
     x = I.normal(T + K, (T, K))
     W = I.normal(E + 7, (E, K), 0.0, 0.05)
@@ -50,3 +51,7 @@ def test_router_logits_topk_needs_logits_off_the_fast_path(ds3, up):
     x, W = I.normal(1, (4, 100)), I.normal(2, (64, 100))
     ib, sb = up(np.zeros((4, 4), np.int32)), up(np.zeros((4, 4), np.float32))
     assert ds3.router_logits_topk(up(x), up(W), None, ib, sb, 4, 100, 64, 4, True) == -1
+    # 128 experts but n_embd not a multiple of 64: also the general path.
+    x2, W2 = I.normal(3, (4, 2080)), I.normal(4, (128, 2080))
+    ib2, sb2 = up(np.zeros((4, 8), np.int32)), up(np.zeros((4, 8), np.float32))
+    assert ds3.router_logits_topk(up(x2), up(W2), None, ib2, sb2, 4, 2080, 128, 8, True) == -1
