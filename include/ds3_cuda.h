@@ -186,6 +186,15 @@ void ds3_cuda_profile_print(const char *label);
 /* Fused ops (new). They replace the sequences named beside each.     */
 /* ------------------------------------------------------------------ */
 
+/* Whole-tensor conversion to fp32 on the device (weights at load time).
+ * Replaces ds3_ref_dequantize_tensor + buffer_write in the engine's
+ * upload_dequantized_fp32 (src/ds3_engine.c:154-179), used for norm weights
+ * stored in another type (:1609-1622). src: n_elements of `type` (F32, F16,
+ * Q8_0, Q4_K, Q6_K; a whole number of blocks) as stored in the file; dst fp32
+ * [n_elements]. Bit-exact with the reference dequant. */
+int ds3_cuda_dequantize_f32(const ds3_cuda_buffer_t *src, ds3_type_t type, uint64_t n_elements,
+                            ds3_cuda_buffer_t *dst);
+
 /* Token-embedding gather + dequant on the device. Replaces the CPU loop
  * upload_token_embeddings (src/ds3_engine.c:273-290, ds3_ref_dequantize_row per
  * token) plus the host->device copy. table: [n_vocab] rows of `row_stride`

@@ -226,3 +226,44 @@ def reference() -> Oracle | None:
     if _ref is None and REF_LIB.exists():
         _ref = Oracle(REF_LIB, "ds3r_")
     return _ref
+
+
+REF_GGUF_LIB = HERE / "_ref" / "libds3gguf.so"
+_ref_gguf = None
+
+
+def reference_gguf(path) -> dict | None:
+    """Header and tensor table of `path` as parsed by the unmodified reference
+    reader (oracle/_ref/libds3gguf.so; None when it has not been built), or
+    {"error": True} when that reader rejects the file. Same keys as
+    oracle.gguf.parse() minus metadata and strides."""
+    global _ref_gguf
+    if _ref_gguf is None:
+        if not REF_GGUF_LIB.exists():
+            return None
+        L = C.CDLL(str(REF_GGUF_LIB))
+        L.ds3rg_open.restype, L.ds3rg_open.argtypes = _P, [C.c_char_p]
+        L.ds3rg_close.restype, L.ds3rg_close.argtypes = None, [_P]
+        L.ds3rg_header.restype, L.ds3rg_header.argtypes = None, [_P, _P]
+        L.ds3rg_tensor.restype, L.ds3rg_tensor.argtypes = _I, [_P, _U64, C.c_char_p, C.c_size_t, _P]
+        _ref_gguf = L
+    L = _ref_gguf
+    h = L.ds3rg_open(str(path).encode())
+    if not h:
+        return {"error": True}
+    try:
+        hd = np.zeros(5, np.uint64)
+        L.ds3rg_header(h, hd.ctypes.data)
+        table = []
+        name = C.create_string_buffer(512)
+        for i in range(int(hd[2])):
+            o = np.zeros(10, np.uint64)
+            assert L.ds3rg_tensor(h, i, name, 512, o.ctypes.data) == 0
+            n_dims = int(o[0])
+            table.append({"name": name.value.decode(), "n_dims": n_dims,
+                          "ne": [int(o[1 + d]) if d < n_dims else 1 for d in range(4)], "type": int(o[5]),
+                          "offset": int(o[6]), "size": int(o[7]), "data_at": int(o[8])})
+        return {"version": int(hd[0]), "alignment": int(hd[1]), "n_metadata": int(hd[3]),
+                "data_offset": int(hd[4]), "tensors": table}
+    finally:
+        L.ds3rg_close(h)

@@ -19,7 +19,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libds3cuda.so"
-SOURCES = ["ds3_cuda.cu", "norm.cu", "embed.cu", "rope.cu", "router.cu", "moe.cu", "moe_route.cu", "router_gemv.cu"]
+SOURCES = ["ds3_cuda.cu", "norm.cu", "embed.cu", "rope.cu", "router.cu", "moe.cu", "moe_route.cu", "router_gemv.cu", "gguf.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -32,20 +32,24 @@ def nvcc() -> str:
 
 HOST_SRC = PKG / "host" / "ds3_chunk_pre.c"
 HOST_BIN = PKG / "host" / "ds3_chunk_pre"
+HOST_PROGRAMS = ("ds3_chunk_pre", "ds3_gguf_info")
 
 
-def build_host() -> Path:
-    """The C host driver, linked against libds3cuda.so (found via rpath)."""
-    if HOST_BIN.exists() and HOST_BIN.stat().st_mtime > max(HOST_SRC.stat().st_mtime, LIB.stat().st_mtime):
-        return HOST_BIN
+def build_host(name: str = "ds3_chunk_pre") -> Path:
+    """A C host program of qw3_b200/host/, linked against libds3cuda.so (found
+    via rpath); builds all of them when called from build()."""
+    src, out = PKG / "host" / f"{name}.c", PKG / "host" / name
+    headers = list((ROOT / "include").glob("*.h"))
+    if out.exists() and out.stat().st_mtime > max(p.stat().st_mtime for p in [src, LIB, *headers]):
+        return out
     cc = shutil.which("gcc") or "cc"
-    cmd = [cc, "-O2", "-std=c11", "-Wall", "-Wextra", "-I", str(ROOT / "include"), str(HOST_SRC),
-           "-L", str(PKG), "-lds3cuda", "-Wl,-rpath,$ORIGIN/..", "-o", str(HOST_BIN)]
+    cmd = [cc, "-O2", "-std=c11", "-Wall", "-Wextra", "-I", str(ROOT / "include"), str(src),
+           "-L", str(PKG), "-lds3cuda", "-Wl,-rpath,$ORIGIN/..", "-o", str(out)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
-        raise RuntimeError("building the C host driver failed")
-    return HOST_BIN
+        raise RuntimeError(f"building the C host program {name} failed")
+    return out
 
 
 def needs_rebuild() -> bool:
@@ -83,5 +87,6 @@ def build(force: bool = False, ptxas_verbose: bool = False) -> Path:
 
 if __name__ == "__main__":
     build(force=True, ptxas_verbose="--verbose-ptxas" in sys.argv)
-    build_host()
+    for prog in HOST_PROGRAMS:
+        build_host(prog)
     print(LIB)

@@ -191,6 +191,15 @@ int rope_freqs(uint32_t head_dim, float theta, float *freq)
 
 }  // namespace
 
+namespace ds3 {
+// Shared with the other host modules of the library (gguf.cpp).
+void report_error(const char *msg)
+{
+    g_last_error = msg;
+    fprintf(stderr, "ds3_cuda: %s\n", msg);
+}
+}  // namespace ds3
+
 extern "C" {
 
 // ------------------------------------------------------------------ lifecycle
@@ -669,6 +678,26 @@ static bool type_row_bytes(ds3_type_t type, uint32_t n_cols, uint64_t *bytes)
     }
 }
 
+int ds3_cuda_dequantize_f32(const ds3_cuda_buffer_t *src, ds3_type_t type, uint64_t n_elements, ds3_cuda_buffer_t *dst)
+{
+    const char *op = "dequantize_f32";
+    if (!ready(op)) return -1;
+    uint64_t rb = 0;
+    const uint32_t n = (uint32_t)n_elements;
+    if (n_elements == 0 || n_elements >= (1ull << 31) || !type_row_bytes(type, n, &rb)) {
+        set_error("%s: unsupported type %d or element count %llu", op, (int)type, (unsigned long long)n_elements);
+        return -1;
+    }
+    if (!need(op, "src", src, (size_t)rb) || !need(op, "dst", dst, (size_t)n_elements * 4) ||
+        !writable(op, "dst", dst))
+        return -1;
+    ProfScope ps(op);
+    return finish(op,
+                  ds3::launch_dequantize(ctx(), (const uint8_t *)dptr(src), (int)type, (int64_t)n_elements,
+                                         (float *)dptr(dst)),
+                  ps);
+}
+
 int ds3_cuda_embed_rms_norm(const ds3_cuda_buffer_t *table, const ds3_cuda_buffer_t *ids,
                             const ds3_cuda_buffer_t *weight, ds3_cuda_buffer_t *hidden_out,
                             ds3_cuda_buffer_t *norm_out, uint32_t n_ids, uint32_t n_cols, uint32_t n_vocab,
@@ -1038,6 +1067,7 @@ int ds3_cuda_selftest_bounded_wait(uint32_t polls)
 }
 
 const char *ds3_cuda_last_error(void) { return g_last_error.c_str(); }
+
 
 uint32_t ds3_cuda_device_errors(void)
 {

@@ -346,6 +346,16 @@ __global__ void embed_generic(const uint8_t *table, int type, uint64_t row_strid
     }
 }
 
+// Whole-tensor conversion to fp32 (weights at load time): element e of a
+// tensor stored as consecutive blocks is element e of one long row.
+__global__ void dequant_tensor_k(const uint8_t *src, int type, int64_t n, float *out)
+{
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x)
+        out[e] = dequant_one(type, src, (int)e);
+}
+
 template <int TYPE, int NB>
 cudaError_t run_fast(const LaunchCtx &c, const EmbedArgs &a)
 {
@@ -414,6 +424,15 @@ cudaError_t launch_embed(const LaunchCtx &c, const uint8_t *table, int type, uin
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || !norm_out) return e;
     return launch_add_rms_norm(c, dst, nullptr, w, nullptr, norm_out, n_cols, n_ids, eps);
+}
+
+cudaError_t launch_dequantize(const LaunchCtx &c, const uint8_t *src, int type, int64_t n, float *out)
+{
+    if (n <= 0) return cudaSuccess;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 32LL * c.n_sm) blocks = 32LL * c.n_sm;
+    launch_k(c, dequant_tensor_k, dim3((unsigned)blocks), dim3(256), src, type, n, out);
+    return cudaGetLastError();
 }
 
 }  // namespace ds3

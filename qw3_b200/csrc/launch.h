@@ -53,6 +53,9 @@ cudaError_t launch_ks(const LaunchCtx &c, void (*k)(KArgs...), dim3 grid, dim3 b
 cudaError_t launch_add_rms_norm(const LaunchCtx &c, const float *x, const float *r, const float *w,
                                 float *sum_out, float *norm_out, int n, int64_t rows, float eps);
 
+// Whole tensor of `type` (F32, F16, Q8_0, Q4_K, Q6_K) to fp32; n < 2^31.
+cudaError_t launch_dequantize(const LaunchCtx &c, const uint8_t *src, int type, int64_t n, float *out);
+
 // Embedding gather (+ RMSNorm when norm_out != nullptr).
 cudaError_t launch_embed(const LaunchCtx &c, const uint8_t *table, int type, uint64_t row_stride,
                          int64_t n_vocab, const int32_t *ids, int64_t n_ids, int n_cols,

@@ -23,6 +23,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 LIB_PATH = PKG / "libds3cuda.so"
 HEADER = ROOT / "include" / "ds3_cuda.h"
+HEADERS = sorted((ROOT / "include").glob("*.h"))
 
 # ds3_type_t (src/ds3.h:201-216 of the reference)
 TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 0, 1, 8, 12, 14
@@ -88,12 +89,28 @@ _SIGS = {
     "last_error": (C.c_char_p, []),
     "device_errors": (_U32, []),
     "selftest_bounded_wait": (_I, [_U32]),
+    "dequantize_f32": (_I, [_P, _I, _U64, _P]),
+    # include/ds3_cuda_gguf.h
+    "gguf_open": (_P, [C.c_char_p]),
+    "gguf_close": (None, [_P]),
+    "gguf_version": (_U32, [_P]),
+    "gguf_alignment": (_U32, [_P]),
+    "gguf_data_offset": (_U64, [_P]),
+    "gguf_n_tensors": (_U64, [_P]),
+    "gguf_n_metadata": (_U64, [_P]),
+    "gguf_tensor": (_I, [_P, _U64, _P]),
+    "gguf_find_tensor": (_I, [_P, C.c_char_p, _P]),
+    "gguf_get_string": (_B, [_P, C.c_char_p, C.POINTER(_P), C.POINTER(_SZ)]),
+    "gguf_get_u32": (_B, [_P, C.c_char_p, C.POINTER(_U32)]),
+    "gguf_get_f32": (_B, [_P, C.c_char_p, C.POINTER(_F)]),
+    "path_weights_load": (_P, [_P, _U32, _B]),
+    "path_weights_free": (None, [_P]),
 }
 
 
 def header_symbols() -> list[str]:
-    """Every ds3_cuda_* function declared in include/ds3_cuda.h."""
-    text = HEADER.read_text()
+    """Every ds3_cuda_* function declared in include/*.h."""
+    text = "\n".join(h.read_text() for h in HEADERS)
     return sorted(set(re.findall(r"\b(ds3_cuda_[a-z0-9_]+)\s*\(", text)))
 
 
@@ -394,3 +411,130 @@ def device_errors() -> int:
 
 def selftest_bounded_wait(polls: int = 1000) -> int:
     return lib().ds3_cuda_selftest_bounded_wait(polls)
+
+
+def dequantize_f32(src, type_, n_elements, dst) -> int:
+    return lib().ds3_cuda_dequantize_f32(_h(src), type_, n_elements, _h(dst))
+
+
+# ---------------------------------------------------------------------------
+# GGUF reader and path-weight binding (include/ds3_cuda_gguf.h)
+# ---------------------------------------------------------------------------
+
+class GgufTensorInfo(C.Structure):
+    """ds3_cuda_gguf_tensor_t"""
+
+    _fields_ = [("name", _P), ("name_len", _U64), ("n_dims", _U32), ("ne", _U64 * 4), ("nb", _U64 * 4),
+                ("type", _U32), ("offset", _U64), ("size", _U64), ("data", _P)]
+
+    def as_dict(self) -> dict:
+        return {"name": C.string_at(self.name, self.name_len).decode(), "n_dims": self.n_dims,
+                "ne": list(self.ne), "nb": list(self.nb), "type": self.type, "offset": self.offset,
+                "size": self.size}
+
+
+class PathWeightsC(C.Structure):
+    """ds3_cuda_path_weights_t"""
+
+    _fields_ = [("n_layer", _U32), ("n_embd", _U32), ("n_vocab", _U32), ("head_dim", _U32), ("n_expert", _U32),
+                ("token_embd_type", _U32), ("token_embd_row_stride", _U64), ("token_embd", _P),
+                ("output_norm", _P), ("attn_norm", C.POINTER(_P)), ("attn_q_norm", C.POINTER(_P)),
+                ("attn_k_norm", C.POINTER(_P)), ("ffn_norm", C.POINTER(_P)), ("ffn_gate_inp", C.POINTER(_P))]
+
+
+class Gguf:
+    """An open GGUF file (ds3_cuda_gguf_open); close() or use as a context manager."""
+
+    def __init__(self, path):
+        self.handle = lib().ds3_cuda_gguf_open(str(path).encode())
+        if not self.handle:
+            raise OSError(last_error())
+
+    def close(self) -> None:
+        if self.handle:
+            lib().ds3_cuda_gguf_close(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def version(self) -> int:
+        return lib().ds3_cuda_gguf_version(self.handle)
+
+    @property
+    def alignment(self) -> int:
+        return lib().ds3_cuda_gguf_alignment(self.handle)
+
+    @property
+    def data_offset(self) -> int:
+        return lib().ds3_cuda_gguf_data_offset(self.handle)
+
+    @property
+    def n_metadata(self) -> int:
+        return lib().ds3_cuda_gguf_n_metadata(self.handle)
+
+    def tensors(self) -> list[dict]:
+        out = []
+        for i in range(lib().ds3_cuda_gguf_n_tensors(self.handle)):
+            t = GgufTensorInfo()
+            assert lib().ds3_cuda_gguf_tensor(self.handle, i, C.byref(t)) == 0
+            out.append(t.as_dict())
+        return out
+
+    def find(self, name: str) -> dict | None:
+        t = GgufTensorInfo()
+        if lib().ds3_cuda_gguf_find_tensor(self.handle, name.encode(), C.byref(t)) != 0:
+            return None
+        return t.as_dict()
+
+    def get_string(self, key: str) -> bytes | None:
+        p, n = _P(), _SZ()
+        if not lib().ds3_cuda_gguf_get_string(self.handle, key.encode(), C.byref(p), C.byref(n)):
+            return None
+        return C.string_at(p.value, n.value)
+
+    def get_u32(self, key: str) -> int | None:
+        v = _U32()
+        return v.value if lib().ds3_cuda_gguf_get_u32(self.handle, key.encode(), C.byref(v)) else None
+
+    def get_f32(self, key: str) -> float | None:
+        v = _F()
+        return v.value if lib().ds3_cuda_gguf_get_f32(self.handle, key.encode(), C.byref(v)) else None
+
+
+class PathWeights:
+    """Device tensors of the fused path bound from a GGUF file
+    (ds3_cuda_path_weights_load). Buffer fields are borrowed handles, freed
+    together by free()."""
+
+    def __init__(self, gguf: Gguf, n_layer: int, require_qk_norm: bool = True):
+        self.handle = lib().ds3_cuda_path_weights_load(gguf.handle, n_layer, require_qk_norm)
+        if not self.handle:
+            raise RuntimeError(last_error())
+        self.c = C.cast(self.handle, C.POINTER(PathWeightsC)).contents
+
+    @staticmethod
+    def _buf(h, nbytes: int) -> "Buffer | None":
+        return _Borrowed(h, nbytes) if h else None
+
+    def layer(self, name: str, i: int, nbytes: int) -> "Buffer | None":
+        return self._buf(getattr(self.c, name)[i], nbytes)
+
+    def free(self) -> None:
+        if self.handle:
+            lib().ds3_cuda_path_weights_free(self.handle)
+            self.handle = None
+
+
+class _Borrowed(Buffer):
+    """A buffer owned by something else (freeing it is a no-op)."""
+
+    def __init__(self, handle: int, nbytes: int):
+        super().__init__(handle, nbytes)
+
+    def free(self) -> None:
+        pass

@@ -83,6 +83,26 @@ def main() -> None:
     res = I.normal(801, (2, 1024))
     wts = sc[:2]
     np.savez_compressed(OUT / "combine.npz", y=y, w=wts, residual=res, out=R.combine(y, wts, res))
+
+    # GGUF reader: the reference reader's header and tensor table for
+    # synthetic model files (tests/gguf_writer.py, deterministic per config).
+    import json
+    import tempfile
+
+    sys.path.insert(0, str(ROOT / "tests"))
+    from gguf_writer import synthetic_model
+
+    cases = []
+    for cfg in (dict(), dict(alignment=256, embd_type=14, norm_type=0), dict(norm_type=8, n_layer=3, seed=3)):
+        g, _ = synthetic_model(**cfg)
+        with tempfile.TemporaryDirectory() as d:
+            p = g.write(Path(d) / "m.gguf")
+            ref = oracle.reference_gguf(p)
+        assert ref and "error" not in ref
+        for t in ref["tensors"]:
+            t.pop("data_at")
+        cases.append({"config": cfg, **ref})
+    (OUT / "gguf_ref_table.json").write_text(json.dumps(cases, indent=1) + "\n")
     print("wrote fixtures to", OUT)
 
 
