@@ -441,6 +441,8 @@ def main():
     # its operands that together exceed L2 (so every launch streams from HBM)
     peak, peak_kind = measured_peak()
     kernels = op_loops(ds3, P, max_over_ranks, barrier, peak)
+    if not args.profile:
+        stream_floor(ds3, kernels, max_over_ranks, barrier)
     tot = sum(k["avg_us"] for k in kernels.values())
     for k in kernels.values():
         k["share"] = round(k["avg_us"] / tot, 4)
@@ -660,6 +662,32 @@ def time_launches(ds3, fns, reps, max_over_ranks, barrier):
     ms = max_over_ranks(ds3.timer_elapsed_ms(2, 3)) / reps
     ds3.graph_free(g)
     return ms
+
+
+def stream_floor(ds3, kernels, max_over_ranks, barrier):
+    """Size-matched streaming floor for each step kernel: ds3_cuda_vec_add (two
+    reads, one write, all loads issued first, PDL) moving the kernel's
+    algorithmic bytes, timed like the kernel itself (back-to-back launches in
+    one graph, operands rotated over sets that exceed L2). At T=512 every op
+    fits in one wave, so even a plain stream stays below the copy peak; this is
+    the time a kernel of that size could reach."""
+    for op, k in kernels.items():
+        nbytes = k["algo_bytes"]
+        n = (nbytes // 12) // 4 * 4
+        if n < 1 << 16:
+            continue  # latency-bound (the router): no meaningful stream
+        nsets = max(2, -(-330_000_000 // (12 * n)))
+        bufs = [[ds3.empty(n * 4) for _ in range(3)] for _ in range(nsets)]
+        for a, b, _ in bufs:
+            ds3.buffer_zero_f32(a, n * 4)
+            ds3.buffer_zero_f32(b, n * 4)
+        fns = [lambda a=a, b=b, c=c: ds3.vec_add(a, b, c, n) for a, b, c in bufs]
+        us = time_launches(ds3, fns, max(40, nsets), max_over_ranks, barrier) * 1e3
+        k["stream_floor_us"] = round(us, 3)
+        k["of_stream_floor"] = round(us / k["avg_us"], 4)
+        for trio in bufs:
+            for x in trio:
+                x.free()
 
 
 def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k):

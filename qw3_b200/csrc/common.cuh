@@ -119,6 +119,15 @@ __device__ __forceinline__ float4 ld_stream_inflight(const float4 *p)
     return v;
 }
 
+// A read-only scalar load kept in program order with the volatile loads around
+// it (so it is issued with them, not after their results are used).
+__device__ __forceinline__ float ld_param_f(const float *p)
+{
+    float v;
+    asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
 // ------------------------------------------------------------------------
 // mbarrier + bulk async copy (TMA, 1-D) helpers.
 // ------------------------------------------------------------------------

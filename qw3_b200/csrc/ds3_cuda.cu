@@ -192,6 +192,38 @@ int rope_freqs(uint32_t head_dim, float theta, float *freq)
 }  // namespace
 
 namespace ds3 {
+constexpr int kMaxPrepared = 256;
+const void *g_prepared[kMaxPrepared];  // kernels already set up
+int g_n_prepared = 0;
+
+// Every kernel launched through launch_k asks for the same L1/shared split.
+// Consecutive kernels with different splits cannot share an SM (it must
+// drain to switch), which defeats programmatic dependent launch; one split
+// for all lets the next kernel's CTAs become resident while the previous
+// kernel finishes. 50 % measured best on the T=512 step (34.1 us vs 35.4 us
+// with the driver's per-kernel choice; 45-55 % alike, 60 % slows the RoPE
+// kernel, 40 % and below starve the TMA-staged norm). DS3_CUDA_CARVEOUT
+// overrides it (-1 leaves the driver's choice).
+void prepare_kernel(const void *k)
+{
+    static const int carve = [] {
+        const char *v = getenv("DS3_CUDA_CARVEOUT");
+        return v ? atoi(v) : 50;
+    }();
+    if (carve < 0) return;
+    for (int i = 0; i < g_n_prepared; i++)
+        if (g_prepared[i] == k) return;
+    cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, carve);
+    if (g_n_prepared < kMaxPrepared) g_prepared[g_n_prepared++] = k;
+}
+
+void keep_driver_carveout(const void *k)
+{
+    for (int i = 0; i < g_n_prepared; i++)
+        if (g_prepared[i] == k) return;
+    if (g_n_prepared < kMaxPrepared) g_prepared[g_n_prepared++] = k;
+}
+
 // Shared with the other host modules of the library (gguf.cpp).
 void report_error(const char *msg)
 {

@@ -15,10 +15,17 @@ struct LaunchCtx {
     bool pdl;       // launch with programmatic stream serialization
 };
 
+// One-time per-kernel set-up before its first launch (shared-memory carveout).
+void prepare_kernel(const void *k);
+// Exempt `k` from the common carveout (call before its first launch): for
+// kernels whose occupancy needs most of the shared memory.
+void keep_driver_carveout(const void *k);
+
 // Launch `k` on c.stream, with the PDL attribute when c.pdl is set.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_k(const LaunchCtx &c, void (*k)(KArgs...), dim3 grid, dim3 block, Args... args)
 {
+    prepare_kernel(reinterpret_cast<const void *>(k));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -36,6 +43,7 @@ cudaError_t launch_k(const LaunchCtx &c, void (*k)(KArgs...), dim3 grid, dim3 bl
 template <typename... KArgs, typename... Args>
 cudaError_t launch_ks(const LaunchCtx &c, void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args)
 {
+    prepare_kernel(reinterpret_cast<const void *>(k));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;

@@ -75,12 +75,17 @@ __global__ void __launch_bounds__(256) swiglu_blk(const float4 *gate, const floa
     pdl_trigger();
     const uint32_t base = blockIdx.x * (256u * U) + threadIdx.x;
     float4 g[U], v[U];
+    float rw[U];
+    // All loads, the routing weight included, are issued before any is used,
+    // so the launch costs one memory round trip.
 #pragma unroll
     for (int k = 0; k < U; k++) {
         const uint32_t u = base + 256u * k;
+        rw[k] = 1.0f;
         if (u < units) {
-            g[k] = ld_stream(gate + u);
-            v[k] = ld_stream(up + u);
+            g[k] = ld_stream_inflight(gate + u);
+            v[k] = ld_stream_inflight(up + u);
+            if (row_w) rw[k] = ld_param_f(row_w + u / cols4);
         }
     }
 #pragma unroll
@@ -90,7 +95,7 @@ __global__ void __launch_bounds__(256) swiglu_blk(const float4 *gate, const floa
         float4 o = make_float4(silu_mul(g[k].x, v[k].x), silu_mul(g[k].y, v[k].y), silu_mul(g[k].z, v[k].z),
                                silu_mul(g[k].w, v[k].w));
         if (row_w) {
-            const float w = __ldg(row_w + u / cols4);
+            const float w = rw[k];
             o = make_float4(__fmul_rn(o.x, w), __fmul_rn(o.y, w), __fmul_rn(o.z, w), __fmul_rn(o.w, w));
         }
         out[u] = o;
@@ -207,6 +212,18 @@ __global__ void combine_scalar(const float *y, const int32_t *y_rows, const floa
 }
 
 // ----------------------------------------------------------------- vec_add
+// Up to 2^31 float4 units: one unit per thread, both loads issued before the
+// add, a non-persistent grid (the same shape as swiglu_blk).
+__global__ void __launch_bounds__(256) vec_add_blk(const float4 *a, const float4 *b, float4 *c, uint32_t n4)
+{
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t i = blockIdx.x * 256u + threadIdx.x;
+    if (i >= n4) return;
+    const float4 x = ld_stream_inflight(a + i), y = ld_stream_inflight(b + i);
+    c[i] = f4_add(x, y);
+}
+
 __global__ void vec_add_vec(const float4 *a, const float4 *b, float4 *c, int64_t n4)
 {
     pdl_wait();
@@ -341,7 +358,10 @@ cudaError_t launch_combine(const LaunchCtx &c, const float *y, const int32_t *y_
 cudaError_t launch_vec_add(const LaunchCtx &c, const float *a, const float *b, float *out, int64_t n)
 {
     if (n <= 0) return cudaSuccess;
-    if (n % 4 == 0 && al16(a) && al16(b) && al16(out))
+    if (n % 4 == 0 && al16(a) && al16(b) && al16(out) && n / 4 < ((int64_t)1 << 31))
+        launch_k(c, vec_add_blk, dim3((unsigned)((n / 4 + 255) / 256)), dim3(256), reinterpret_cast<const float4 *>(a),
+                 reinterpret_cast<const float4 *>(b), reinterpret_cast<float4 *>(out), (uint32_t)(n / 4));
+    else if (n % 4 == 0 && al16(a) && al16(b) && al16(out))
         launch_k(c, vec_add_vec, dim3(grid_for(c, n / 4, 256, 16)), dim3(256), 
             reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b),
             reinterpret_cast<float4 *>(out), n / 4);

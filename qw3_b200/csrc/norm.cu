@@ -66,19 +66,21 @@ __global__ void __launch_bounds__(128) add_rms_norm_warp(const float *x, const f
 // a persistent grid of up to kBulkCtasPerSm CTAs per SM strides over rows.
 constexpr int kBulkCtasPerSm = 7;
 
-template <int VPL>
+template <int VPL, int NS>
 __global__ void __launch_bounds__(32) add_rms_norm_bulk(const float *x, const float *r, const float *w,
                                                         float *sum_out, float *norm_out, int64_t rows,
                                                         float eps, unsigned *err)
 {
     constexpr int n = VPL * 128;
     constexpr uint32_t kRowBytes = n * sizeof(float);
-    __shared__ __align__(128) float4 buf[2][2][n / 4];  // [slot][x|r][row]
-    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ __align__(128) float4 buf[NS][2][n / 4];  // [slot][x|r][row]
+    __shared__ __align__(128) float4 ws[n / 4];           // the norm weight
+    __shared__ __align__(8) uint64_t bars[3];             // row slots 0/1, weight
     const int lane = threadIdx.x;
     if (lane == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
+        mbar_init(&bars[2], 1);
         mbar_init_fence();
     }
     __syncwarp();
@@ -96,19 +98,31 @@ __global__ void __launch_bounds__(32) add_rms_norm_bulk(const float *x, const fl
             if (r) bulk_g2s(buf[s][1], r + row * n, kRowBytes, &bars[s]);
         }
     };
+    // The weight comes in by one bulk copy issued with the first row, so the
+    // normed stores cost no second round trip.
+    if (lane == 0) {
+        mbar_expect_tx(&bars[2], kRowBytes);
+        bulk_g2s(ws, w, kRowBytes, &bars[2]);
+    }
     uint32_t parity = 0;
     int slot = 0;
+    bool w_ready = false;
     issue(0, cur);
-    const float4 *w4 = reinterpret_cast<const float4 *>(w);
-    for (; cur < rows; cur += stride, slot ^= 1) {
+    for (; cur < rows; cur += stride, slot ^= (NS - 1)) {
         const int64_t nxt = cur + stride;
-        if (nxt < rows) issue(slot ^ 1, nxt);
-        const bool done = __all_sync(kFull, mbar_wait(&bars[slot], (parity >> slot) & 1u, kWaitLimit));
+        if (NS == 2 && nxt < rows) issue(slot ^ 1, nxt);
+        bool done = __all_sync(kFull, mbar_wait(&bars[slot], (parity >> slot) & 1u, kWaitLimit));
         parity ^= 1u << slot;
+        if (done && !w_ready) {
+            done = __all_sync(kFull, mbar_wait(&bars[2], 0, kWaitLimit));
+            w_ready = done;
+        }
         if (!done) {
+            // Record the timeout, let this CTA's copies land (bounded), stop.
             if (lane == 0) flag_error(err, kErrWaitTimeout);
             mbar_wait(&bars[slot], ((parity >> slot) & 1u) ^ 1u, kWaitLimit);
-            if (nxt < rows) mbar_wait(&bars[slot ^ 1], (parity >> (slot ^ 1)) & 1u, kWaitLimit);
+            if (NS == 2 && nxt < rows) mbar_wait(&bars[slot ^ 1], (parity >> (slot ^ 1)) & 1u, kWaitLimit);
+            mbar_wait(&bars[2], 0, kWaitLimit);
             return;
         }
         float4 v[VPL];
@@ -118,6 +132,7 @@ __global__ void __launch_bounds__(32) add_rms_norm_bulk(const float *x, const fl
             if (r) v[i] = f4_add(v[i], buf[slot][1][i * 32 + lane]);
         }
         __syncwarp();  // slot free for the copy issued next iteration
+        if (NS == 1 && nxt < rows) issue(slot, nxt);
         float ss = 0.0f;
 #pragma unroll
         for (int i = 0; i < VPL; i++) ss = f4_sumsq(v[i], ss);
@@ -130,7 +145,7 @@ __global__ void __launch_bounds__(32) add_rms_norm_bulk(const float *x, const fl
         }
         float4 *no = reinterpret_cast<float4 *>(norm_out + cur * n);
 #pragma unroll
-        for (int i = 0; i < VPL; i++) no[i * 32 + lane] = f4_norm(v[i], inv, ld_param(w4 + i * 32 + lane));
+        for (int i = 0; i < VPL; i++) no[i * 32 + lane] = f4_norm(v[i], inv, ws[i * 32 + lane]);
     }
 }
 
@@ -139,9 +154,16 @@ cudaError_t run_bulk(const LaunchCtx &c, const float *x, const float *r, const f
                      float *norm_out, int64_t rows, float eps)
 {
     const int64_t cap = (int64_t)c.n_sm * kBulkCtasPerSm;
-    const int64_t blocks = rows < cap ? rows : cap;
-    launch_k(c, add_rms_norm_bulk<VPL>, dim3((unsigned)blocks), dim3(32), x, r, w, sum_out, norm_out, rows, eps,
-             c.err);
+    // One row per CTA (rows <= cap): one slot, half the shared memory, so
+    // more CTAs fit at a given carveout; otherwise two slots overlap a CTA's
+    // next row with the current one.
+    if (rows <= cap) {
+        launch_k(c, add_rms_norm_bulk<VPL, 1>, dim3((unsigned)rows), dim3(32), x, r, w, sum_out, norm_out, rows, eps,
+                 c.err);
+    } else {
+        launch_k(c, add_rms_norm_bulk<VPL, 2>, dim3((unsigned)cap), dim3(32), x, r, w, sum_out, norm_out, rows, eps,
+                 c.err);
+    }
     return cudaGetLastError();
 }
 

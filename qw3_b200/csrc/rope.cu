@@ -112,6 +112,7 @@ struct HeadSlice<__half> {
 // the RMS sum is 3 shuffles and the rotation needs no data exchange.
 constexpr int kTileTok = 2;
 constexpr int kTileWarps = 9;
+constexpr int kTok1Warps = 5;  // one-token tiles: up to 10 groups of 4 heads
 
 // fp16 copy of a lane's 16 values into a 128-wide cache row, at the element
 // positions HeadSlice<T> uses for that lane.
@@ -140,33 +141,38 @@ __device__ __forceinline__ void cache_store(__half *row, int j, const float *lo,
 template <bool KV>
 __host__ __device__ constexpr int tile_warps() { return KV ? 10 : 9; }
 
-template <typename T, bool KV>
-__global__ void __launch_bounds__(tile_warps<KV>() * 32, (sizeof(T) == 2 && !KV) ? 4 : 3) qk_norm_rope_tile(
+template <typename T, bool KV, int W>
+__host__ __device__ constexpr int tile_min_blocks() { return W <= 5 ? 5 : ((sizeof(T) == 2 && !KV) ? 4 : 3); }
+
+template <typename T, bool KV, int TT = kTileTok, int W = tile_warps<KV>()>
+__global__ void __launch_bounds__(W * 32, tile_min_blocks<T, KV, W>()) qk_norm_rope_tile(
     const T *q_src, T *q_dst, const T *k_src, T *k_dst, const float *q_w, const float *k_w,
     const int32_t *pos, int64_t rows, int nq, int nk, const __grid_constant__ FreqTable ft, float eps,
     int do_norm, const T *v_src, __half *k_cache, __half *v_cache, int max_seq, unsigned *err)
 {
     constexpr int kMaxG = 2;
-    constexpr int kW = tile_warps<KV>();
-    __shared__ __align__(16) float cs[kTileTok][64];
-    __shared__ __align__(16) float sn[kTileTok][64];
+    constexpr int kW = W;
+    __shared__ __align__(16) float cs[TT][64];
+    __shared__ __align__(16) float sn[TT][64];
     __shared__ __align__(16) float wq[128];
     __shared__ __align__(16) float wk[128];
 
     const int tid = threadIdx.x;
     if (do_norm) {  // static parameters: safe to read before the wait
-        if (tid < 128) wq[tid] = q_w[tid];
-        else if (tid < 256 && nk > 0) wk[tid - 128] = k_w[tid - 128];
+        for (int i = tid; i < 256; i += W * 32) {
+            if (i < 128) wq[i] = q_w[i];
+            else if (nk > 0) wk[i - 128] = k_w[i - 128];
+        }
     }
     pdl_wait();
     pdl_trigger();
 
-    const int64_t t0 = (int64_t)blockIdx.x * kTileTok;
+    const int64_t t0 = (int64_t)blockIdx.x * TT;
     const int lane = tid & 31, warp = tid >> 5;
     const int sub = lane >> 3;  // head within the group of 4
     const int j = lane & 7;     // slice of the head
     const int nh = nq + nk + (KV ? nk : 0);
-    const int n_heads = kTileTok * nh;
+    const int n_heads = TT * nh;
     const int n_groups = (n_heads + 3) >> 2;
 
     float lo[kMaxG][8], hi[kMaxG][8];
@@ -208,7 +214,7 @@ __global__ void __launch_bounds__(tile_warps<KV>() * 32, (sizeof(T) == 2 && !KV)
     }
 
     // cos/sin of this tile's tokens, computed while the loads above are in flight
-    if (tid < kTileTok * 64) {
+    if (tid < TT * 64) {
         const int tl = tid >> 6, i = tid & 63;
         const int64_t t = t0 + tl;
         float s = 0.0f, c = 1.0f;
@@ -301,8 +307,10 @@ __global__ void __launch_bounds__(W * 32) qk_norm_rope_bulk(
     const int nh = nq + nk;
     const size_t stage_elems = (size_t)TT * nh * 128;
     if (do_norm) {  // static parameters: safe to read before the wait
-        if (tid < 128) wq[tid] = q_w[tid];
-        else if (tid < 256 && nk > 0) wk[tid - 128] = k_w[tid - 128];
+        for (int i = tid; i < 256; i += W * 32) {
+            if (i < 128) wq[i] = q_w[i];
+            else if (nk > 0) wk[i - 128] = k_w[i - 128];
+        }
     }
     if (tid == 0) {
         for (int s = 0; s < NS; s++) mbar_init(&bars[s], 1);
@@ -437,6 +445,9 @@ cudaError_t run_bulk(const LaunchCtx &c, const void *qs, void *qd, const void *k
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         configured = smem;
+        // Its occupancy needs most of the shared memory (0.73 vs 0.64 of the
+        // copy peak at T=32768 under the common 50 % carveout).
+        keep_driver_carveout(reinterpret_cast<const void *>(qk_norm_rope_bulk<T, TT, NS, W>));
     }
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_bulk<T, TT, NS, W>, W * 32, smem);
@@ -522,6 +533,15 @@ cudaError_t run(const LaunchCtx &c, const void *qs, void *qd, const void *ks, vo
                 int nk, int hd, int use_hd128, const FreqTable &ft, float eps, int do_norm)
 {
     if (use_hd128) {
+        // One token per CTA (5 warps, 2 groups of 4 heads each) whenever the
+        // token's heads fit: 512 small CTAs keep more loads in flight per SM
+        // than 256 two-token CTAs (T=512: 5.35 vs 5.88 us; T=32768 alike).
+        if ((nq + nk + 3) / 4 <= 2 * kTok1Warps) {
+            launch_k(c, qk_norm_rope_tile<T, false, 1, kTok1Warps>, dim3((unsigned)rows), dim3(kTok1Warps * 32),
+                     (const T *)qs, (T *)qd, (const T *)ks, (T *)kd, q_w, k_w, pos, rows, nq, nk, ft, eps, do_norm,
+                     (const T *)nullptr, (__half *)nullptr, (__half *)nullptr, 0, c.err);
+            return cudaGetLastError();
+        }
         const int64_t blocks = (rows + kTileTok - 1) / kTileTok;
         launch_k(c, qk_norm_rope_tile<T, false>, dim3((unsigned)blocks), dim3(kTileWarps * 32), (const T *)qs,
                  (T *)qd, (const T *)ks, (T *)kd, q_w, k_w, pos, rows, nq, nk, ft, eps, do_norm, (const T *)nullptr,
@@ -589,6 +609,18 @@ cudaError_t launch_qk_norm_rope_kv(const LaunchCtx &c, void *q, void *k, const v
     if ((al & 15u) || groups > kW * 2 || rows > 0x7fffffffLL) return cudaErrorInvalidValue;
     FreqTable ft;
     for (int i = 0; i < 64; i++) ft.f[i] = freq[i];
+    if ((nq + 2 * nk + 3) / 4 <= 2 * kTok1Warps) {
+        const dim3 grid((unsigned)rows), block(kTok1Warps * 32);
+        if (storage)
+            launch_k(c, qk_norm_rope_tile<__half, true, 1, kTok1Warps>, grid, block, (const __half *)q, (__half *)q,
+                     (const __half *)k, (__half *)k, q_w, k_w, pos, rows, nq, nk, ft, eps, 1, (const __half *)v,
+                     (__half *)k_cache, (__half *)v_cache, max_seq, c.err);
+        else
+            launch_k(c, qk_norm_rope_tile<float, true, 1, kTok1Warps>, grid, block, (const float *)q, (float *)q,
+                     (const float *)k, (float *)k, q_w, k_w, pos, rows, nq, nk, ft, eps, 1, (const float *)v,
+                     (__half *)k_cache, (__half *)v_cache, max_seq, c.err);
+        return cudaGetLastError();
+    }
     const int64_t blocks = (rows + kTileTok - 1) / kTileTok;
     if (storage)
         launch_k(c, qk_norm_rope_tile<__half, true>, dim3((unsigned)blocks), dim3(kW * 32),
