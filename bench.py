@@ -75,12 +75,12 @@ STEP_BYTES = sum(ALGO_BYTES.values())
 # the algorithmic input bytes; the outputs of one T=512 launch are still in
 # L2 when it ends, so no write traffic is attributed to the launch itself.
 NCU_TRAFFIC = {
-    "embed_rms_norm": 636032,
-    "qk_norm_rope": 9459712,
-    "add_rms_norm": 8411776,
-    "router_softmax_topk": 270336,
-    "swiglu": 25189376,
-    "moe_combine_residual": 37771008,
+    "embed_rms_norm": 635648,
+    "qk_norm_rope": 9456896,
+    "add_rms_norm": 8411648,
+    "router_softmax_topk": 270080,
+    "swiglu": 25189632,
+    "moe_combine_residual": 37773056,
 }
 
 CONFIG = {
