@@ -79,6 +79,47 @@ __device__ __forceinline__ float norm_mul(float x, float inv, float w)
 
 __device__ __forceinline__ float sq_acc(float acc, float x) { return fmaf(x, x, acc); }
 
+// Packed fp32 pairs (the f32x2 instructions of sm_100): each half is one IEEE
+// round-to-nearest operation, bit-identical to __fmul_rn / __fadd_rn /
+// __fsub_rn / fmaf applied to that half alone. Operands already in adjacent
+// registers need no moves.
+__device__ __forceinline__ unsigned long long f2_bits(float2 a)
+{
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a.x), "f"(a.y));
+    return r;
+}
+__device__ __forceinline__ float2 f2_val(unsigned long long r)
+{
+    float2 v;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+    return v;
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b)
+{
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_val(d);
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b)
+{
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_val(d);
+}
+__device__ __forceinline__ float2 sub2_rn(float2 a, float2 b)
+{
+    unsigned long long d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_val(d);
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c)
+{
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+    return f2_val(d);
+}
+
 __device__ __forceinline__ float4 f4_add(float4 a, float4 b)
 {
     return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y),

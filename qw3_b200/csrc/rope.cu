@@ -44,11 +44,19 @@ __device__ __forceinline__ float rot_hi(float own, float other, float c, float s
 // load/store instruction of the 8 lanes covers 128 contiguous bytes.
 //   fp32: lo = {4j..4j+3, 32+4j..32+4j+3}, pair index of lo[e] = pidx(j, e)
 //   fp16: lo = {8j..8j+7}
+// Lane-major tables of per-pair values (cos, sin, norm weight): the value
+// lane j needs for its element e sits at tab_pos(j, e), so a lane reads its 8
+// values with two 128-bit loads, and 8 lanes together read 128 contiguous
+// bytes (no bank conflicts).
+__host__ __device__ constexpr int tab_pos(int j, int e) { return ((e >> 2) * 8 + j) * 4 + (e & 3); }
+
 template <typename T>
 struct HeadSlice;
 template <>
 struct HeadSlice<float> {
     __device__ static int pidx(int j, int e) { return (e < 4) ? 4 * j + e : 32 + 4 * j + (e - 4); }
+    // Position of pair index p in a lane-major table (see tab_pos).
+    __device__ static int tab(int p) { return p < 32 ? tab_pos(p >> 2, p & 3) : tab_pos((p - 32) >> 2, 4 + (p & 3)); }
     __device__ static void load(const float *head, int j, float *lo, float *hi)
     {
         const float4 *q = reinterpret_cast<const float4 *>(head);
@@ -71,6 +79,7 @@ struct HeadSlice<float> {
 template <>
 struct HeadSlice<__half> {
     __device__ static int pidx(int j, int e) { return 8 * j + e; }
+    __device__ static int tab(int p) { return tab_pos(p >> 3, p & 7); }
     __device__ static void unpack(uint4 u, float *v)
     {
         const unsigned w[4] = {u.x, u.y, u.z, u.w};
@@ -278,6 +287,58 @@ __device__ __forceinline__ void head_from_smem(const __half *head, int j, float 
     HeadSlice<__half>::unpack(q[8 + j], hi);
 }
 
+// Norm (optional) and rotation of one lane's 8 + 8 elements from lane-major
+// tables: w = [lo 64 | hi 64] weights, c / sn = 64 cos / sin. The products
+// and sums are those of norm_mul / rot_lo / rot_hi, two lanes of work per
+// packed f32x2 instruction, so every element is rounded as by the scalar
+// code; only the sum of squares is accumulated in four partial sums.
+__device__ __forceinline__ void norm_rotate_packed(float *xl, float *xh, int j, const float *w, const float *c,
+                                                   const float *sn, bool do_norm, float eps)
+{
+    if (do_norm) {
+        float2 al = make_float2(0.f, 0.f), ah = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            const float2 l = make_float2(xl[e], xl[e + 1]), h = make_float2(xh[e], xh[e + 1]);
+            al = fma2_rn(l, l, al);
+            ah = fma2_rn(h, h, ah);
+        }
+        float ss = (al.x + al.y) + (ah.x + ah.y);
+        ss += __shfl_xor_sync(kFull, ss, 1);
+        ss += __shfl_xor_sync(kFull, ss, 2);
+        ss += __shfl_xor_sync(kFull, ss, 4);
+        const float inv = rms_inv_pow2<128>(ss, eps);
+        const float2 i2 = make_float2(inv, inv);
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            const float4 wl = *reinterpret_cast<const float4 *>(w + tab_pos(j, 4 * q));
+            const float4 wh = *reinterpret_cast<const float4 *>(w + 64 + tab_pos(j, 4 * q));
+            float2 a = mul2_rn(mul2_rn(make_float2(xl[4 * q], xl[4 * q + 1]), i2), make_float2(wl.x, wl.y));
+            float2 b = mul2_rn(mul2_rn(make_float2(xl[4 * q + 2], xl[4 * q + 3]), i2), make_float2(wl.z, wl.w));
+            xl[4 * q] = a.x; xl[4 * q + 1] = a.y; xl[4 * q + 2] = b.x; xl[4 * q + 3] = b.y;
+            a = mul2_rn(mul2_rn(make_float2(xh[4 * q], xh[4 * q + 1]), i2), make_float2(wh.x, wh.y));
+            b = mul2_rn(mul2_rn(make_float2(xh[4 * q + 2], xh[4 * q + 3]), i2), make_float2(wh.z, wh.w));
+            xh[4 * q] = a.x; xh[4 * q + 1] = a.y; xh[4 * q + 2] = b.x; xh[4 * q + 3] = b.y;
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+        const float4 c4 = *reinterpret_cast<const float4 *>(c + tab_pos(j, 4 * q));
+        const float4 s4 = *reinterpret_cast<const float4 *>(sn + tab_pos(j, 4 * q));
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int e = 4 * q + 2 * h;
+            const float2 cc = h ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
+            const float2 ss = h ? make_float2(s4.z, s4.w) : make_float2(s4.x, s4.y);
+            const float2 lo = make_float2(xl[e], xl[e + 1]), hi = make_float2(xh[e], xh[e + 1]);
+            const float2 yl = sub2_rn(mul2_rn(lo, cc), mul2_rn(hi, ss));  // x0*c - x1*s
+            const float2 yh = add2_rn(mul2_rn(lo, ss), mul2_rn(hi, cc));  // x0*s + x1*c
+            xl[e] = yl.x; xl[e + 1] = yl.y;
+            xh[e] = yh.x; xh[e + 1] = yh.y;
+        }
+    }
+}
+
 // head_dim = 128, large token counts: a persistent CTA streams tiles of TT
 // consecutive tokens. A tile's q rows (and its k rows) are contiguous in
 // memory, so each is one 1-D bulk async copy (TMA, no multicast) into an
@@ -307,9 +368,10 @@ __global__ void __launch_bounds__(W * 32) qk_norm_rope_bulk(
     const int nh = nq + nk;
     const size_t stage_elems = (size_t)TT * nh * 128;
     if (do_norm) {  // static parameters: safe to read before the wait
-        for (int i = tid; i < 256; i += W * 32) {
-            if (i < 128) wq[i] = q_w[i];
-            else if (nk > 0) wk[i - 128] = k_w[i - 128];
+        for (int i = tid; i < 256; i += W * 32) {  // lane-major halves (tab)
+            const int m = i & 127, at = (m & 64) + HeadSlice<T>::tab(m & 63);
+            if (i < 128) wq[at] = q_w[m];
+            else if (nk > 0) wk[at] = k_w[m];
         }
     }
     if (tid == 0) {
@@ -363,8 +425,8 @@ __global__ void __launch_bounds__(W * 32) qk_norm_rope_bulk(
             if (idx < TT * 64) {
                 float sv, cv;
                 sincosf(__fmul_rn((float)pcur[k], ft.f[idx & 63]), &sv, &cv);
-                cs[idx >> 6][idx & 63] = cv;
-                sn[idx >> 6][idx & 63] = sv;
+                cs[idx >> 6][HeadSlice<T>::tab(idx & 63)] = cv;
+                sn[idx >> 6][HeadSlice<T>::tab(idx & 63)] = sv;
             }
         }
         const bool ok = __syncthreads_and(mbar_wait(&bars[s], (parity >> s) & 1u, kWaitLimit));
@@ -391,39 +453,17 @@ __global__ void __launch_bounds__(W * 32) qk_norm_rope_bulk(
             const int h = 4 * g + sub;
             const bool act = h < n_heads;
             const int hc = act ? h : 0;
-            const int tl = hc / nh, hh = hc - tl * nh;
+            // token within the tile: no integer division for 1- and 2-token tiles
+            const int tl = TT == 1 ? 0 : TT == 2 ? (hc >= nh ? 1 : 0) : hc / nh, hh = hc - tl * nh;
             const bool is_k = hh >= nq;
             const T *src = is_k ? sk + (size_t)(tl * nk + (hh - nq)) * 128 : sq + (size_t)(tl * nq + hh) * 128;
             float xl[8], xh[8];
             head_from_smem(src, j, xl, xh);
-            if (do_norm) {
-                float ss = 0.0f;
-#pragma unroll
-                for (int e = 0; e < 8; e++) ss = sq_acc(sq_acc(ss, xl[e]), xh[e]);
-                ss += __shfl_xor_sync(kFull, ss, 1);
-                ss += __shfl_xor_sync(kFull, ss, 2);
-                ss += __shfl_xor_sync(kFull, ss, 4);
-                const float inv = rms_inv_pow2<128>(ss, eps);
-                const float *w = is_k ? wk : wq;
-#pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    const int pi = HeadSlice<T>::pidx(j, e);
-                    xl[e] = norm_mul(xl[e], inv, w[pi]);
-                    xh[e] = norm_mul(xh[e], inv, w[pi + 64]);
-                }
-            }
-            float yl[8], yh[8];
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                const int pi = HeadSlice<T>::pidx(j, e);
-                const float c = cs[tl][pi], sv = sn[tl][pi];
-                yl[e] = rot_lo(xl[e], xh[e], c, sv);
-                yh[e] = rot_hi(xh[e], xl[e], c, sv);
-            }
+            norm_rotate_packed(xl, xh, j, is_k ? wk : wq, cs[tl], sn[tl], do_norm, eps);
             if (act) {
                 const int64_t t = t0 + tl;
                 T *dst = is_k ? k_dst + (t * nk + (hh - nq)) * 128 : q_dst + (t * nq + hh) * 128;
-                HeadSlice<T>::store(dst, j, yl, yh);
+                HeadSlice<T>::store(dst, j, xl, xh);
             }
         }
         __syncthreads();  // stage s and cs/sn are free
