@@ -341,6 +341,8 @@ def main():
     ap.add_argument("--only-configs", action="store_true",
                     help="run only the per-config kernels (a short command for ncu captures)")
     ap.add_argument("--profile", action="store_true", help="short run for ncu: no e2e, baseline or configs")
+    ap.add_argument("--rope-f16", type=int, default=0, metavar="T",
+                    help="time only QK-norm+RoPE with fp16 storage on T tokens (a small case for ncu)")
     ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between ops (1/0)")
     args = ap.parse_args()
     rank, world, local = dist_env()
@@ -383,6 +385,12 @@ def main():
         t = torch.tensor([x], dtype=torch.float64, device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t.item())
+
+    if args.rope_f16:
+        line = run_rope_f16(ds3, args.rope_f16, max_over_ranks, barrier)
+        if rank == 0:
+            emit(line)
+        return 0
 
     # ---- inputs: table shared by all steps, S rotating sets of activations
     table_host = I.q4k_table(V, H, 1)
@@ -688,6 +696,27 @@ def stream_floor(ds3, kernels, max_over_ranks, barrier):
         for trio in bufs:
             for x in trio:
                 x.free()
+
+
+def run_rope_f16(ds3, T, max_over_ranks, barrier):
+    """QK-norm + RoPE with fp16 storage on T tokens, in place, over three
+    input sets (together larger than L2 from T = 8192 up)."""
+    sets = []
+    for i in range(3):
+        q = ds3.upload(I.normal(7000 + i, (T, NQ, HD)).astype(np.float16))
+        k = ds3.upload(I.normal(7100 + i, (T, NK, HD)).astype(np.float16))
+        sets.append((q, k))
+    qw, kw = ds3.upload(I.gamma(HD, 7200)), ds3.upload(I.gamma(HD, 7201))
+    pos = ds3.upload(np.arange(T, dtype=np.int32))
+    fns = [lambda q=q, k=k: ds3.qk_norm_rope(q, k, qw, kw, pos, T, NQ, NK, HD, I.ROPE_THETA, I.NORM_EPS,
+                                             ds3.TYPE_F16) for q, k in sets]
+    ms = time_launches(ds3, fns, 12, max_over_ranks, barrier)
+    nbytes = T * (4 * (NQ + NK) * HD + 4)
+    peak, _ = measured_peak()
+    for b in [x for qk in sets for x in qk] + [qw, kw, pos]:
+        b.free()
+    return {"workload": f"qk_norm_rope_f16_T{T}", "us": round(ms * 1e3, 3), "algo_bytes": nbytes,
+            "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1), "frac_of_measured_peak": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)}
 
 
 def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k):
