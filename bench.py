@@ -180,7 +180,7 @@ class ClockSampler:
         0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.005):
+    def __init__(self, device_index: int, period_s: float = 0.0005):
         self.samples, self.reasons = [], 0
         self.max_mhz = None
         self.period = period_s
@@ -217,8 +217,7 @@ class ClockSampler:
         if self._t:
             self._stop.set()
             self._t.join()
-            if not self.samples:
-                self._sample()
+            self._sample()  # the end of the timed region, however short it was
 
     def summary(self):
         if not self.nv or not self.samples:
