@@ -8,10 +8,10 @@
 // token's k slots in order) and their scores alongside; counts[ex] = j.
 //
 // One CTA per expert, all experts in parallel. CTA ex walks the T*K
-// (token, slot) entries in entry order, 1024 at a time (8 chunks of loads
-// issued before any is used): a ballot gives each warp's hits and each hit's
-// rank, a 32-value warp scan the offsets of earlier warps, and a running base
-// carries over between chunks. Every hit lands at ids[ex*cap + j] in the
+// (token, slot) entries in entry order, 4096 at a time, 4 consecutive entries
+// per thread: each thread counts its hits, one CTA-wide exclusive scan (two
+// warp scans) gives every hit its rank, and a running base carries over
+// between passes. Every hit lands at ids[ex*cap + j] in the
 // engine's order, with no atomics and no memory beyond the outputs.
 // slot_of[t*K+k] = ex*cap + j is written by the CTA of the entry's expert; it
 // is the row map moe_combine_residual takes to read expert outputs laid out
@@ -24,7 +24,8 @@ namespace {
 
 constexpr int kRouteThreads = 1024;
 constexpr int kRouteWarps = kRouteThreads / 32;
-constexpr int kPrefetch = 8;
+constexpr int kPerThread = 4;                              // consecutive entries per thread
+constexpr int kRouteChunk = kRouteThreads * kPerThread;    // 4096 = 512 tokens x top-8 in one pass
 
 __global__ void __launch_bounds__(kRouteThreads) moe_expert_lists_k(
     const int32_t *idx, const float *scores, int32_t *counts, int32_t *ids, float *gscores, int32_t *slot_of,
@@ -36,55 +37,67 @@ __global__ void __launch_bounds__(kRouteThreads) moe_expert_lists_k(
     pdl_trigger();
     const int ex = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const unsigned lt_mask = (1u << lane) - 1u;
     int64_t base = 0;
-    for (int64_t s0 = 0; s0 < n_entries; s0 += (int64_t)kPrefetch * kRouteThreads) {
-        int ev[kPrefetch];
+    for (int64_t s0 = 0; s0 < n_entries; s0 += kRouteChunk) {
+        // Entries s0 + 4*tid .. +3: ids and scores are loaded together, before
+        // either is used, so the pass costs one memory round trip.
+        const int64_t i0 = s0 + (int64_t)kPerThread * tid;
+        int ev[kPerThread];
+        float sv[kPerThread];
 #pragma unroll
-        for (int c = 0; c < kPrefetch; c++) {
-            const int64_t i = s0 + (int64_t)c * kRouteThreads + tid;
-            ev[c] = i < n_entries ? idx[i] : -1;
-            if (ex == 0 && i < n_entries && (ev[c] < 0 || ev[c] >= n_expert)) {
+        for (int c = 0; c < kPerThread; c++) {
+            const bool in = i0 + c < n_entries;
+            ev[c] = in ? idx[i0 + c] : -1;
+            sv[c] = in ? scores[i0 + c] : 0.0f;
+        }
+        int mine = 0;
+#pragma unroll
+        for (int c = 0; c < kPerThread; c++) {
+            mine += ev[c] == ex;
+            if (ex == 0 && i0 + c < n_entries && (ev[c] < 0 || ev[c] >= n_expert)) {
+                flag_error(err, kErrBadId);
+                if (slot_of) slot_of[i0 + c] = -1;
+            }
+        }
+        // Exclusive scan of the hit counts over the CTA, in entry order.
+        int inc = mine;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(kFull, inc, o);
+            if (lane >= o) inc += y;
+        }
+        if (lane == 31) wpre[warp] = inc;
+        __syncthreads();
+        if (warp == 0) {
+            const int v = wpre[lane];
+            int w = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(kFull, w, o);
+                if (lane >= o) w += y;
+            }
+            wpre[lane] = w - v;
+            if (lane == 31) total = w;
+        }
+        __syncthreads();
+        int64_t j = base + wpre[warp] + (inc - mine);
+#pragma unroll
+        for (int c = 0; c < kPerThread; c++) {
+            if (ev[c] != ex) continue;
+            const int64_t i = i0 + c;
+            if (j < cap) {
+                const int64_t slot = (int64_t)ex * cap + j;
+                ids[slot] = (int32_t)(i / n_used);
+                gscores[slot] = sv[c];
+                if (slot_of) slot_of[i] = (int32_t)slot;
+            } else {
                 flag_error(err, kErrBadId);
                 if (slot_of) slot_of[i] = -1;
             }
+            j++;
         }
-#pragma unroll
-        for (int c = 0; c < kPrefetch; c++) {
-            const int64_t c0 = s0 + (int64_t)c * kRouteThreads;
-            if (c0 >= n_entries) break;  // uniform across the CTA
-            const bool hit = ev[c] == ex;
-            const unsigned bal = __ballot_sync(kFull, hit);
-            if (lane == 0) wpre[warp] = __popc(bal);
-            __syncthreads();
-            if (warp == 0) {  // exclusive scan of the 32 warp counts
-                const int v = wpre[lane];
-                int inc = v;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int y = __shfl_up_sync(kFull, inc, o);
-                    if (lane >= o) inc += y;
-                }
-                wpre[lane] = inc - v;
-                if (lane == 31) total = inc;
-            }
-            __syncthreads();
-            if (hit) {
-                const int64_t i = c0 + tid;
-                const int64_t j = base + wpre[warp] + __popc(bal & lt_mask);
-                if (j < cap) {
-                    const int64_t slot = (int64_t)ex * cap + j;
-                    ids[slot] = (int32_t)(i / n_used);
-                    gscores[slot] = scores[i];
-                    if (slot_of) slot_of[i] = (int32_t)slot;
-                } else {
-                    flag_error(err, kErrBadId);
-                    if (slot_of) slot_of[i] = -1;
-                }
-            }
-            base += total;
-            __syncthreads();  // wpre / total are rewritten by the next chunk
-        }
+        base += total;
+        __syncthreads();  // wpre / total are rewritten by the next pass
     }
     if (tid == 0) counts[ex] = (int32_t)base;
 }
