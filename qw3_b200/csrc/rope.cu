@@ -270,16 +270,8 @@ __global__ void __launch_bounds__(W * 32, tile_min_blocks<T, KV, W>()) qk_norm_r
     }
 }
 
-// Shared-memory counterparts of HeadSlice::load (same element layout).
-__device__ __forceinline__ void head_from_smem(const float *head, int j, float *lo, float *hi)
-{
-    const float4 *q = reinterpret_cast<const float4 *>(head);
-    const float4 a = q[j], b = q[8 + j], c = q[16 + j], d = q[24 + j];
-    lo[0] = a.x; lo[1] = a.y; lo[2] = a.z; lo[3] = a.w;
-    lo[4] = b.x; lo[5] = b.y; lo[6] = b.z; lo[7] = b.w;
-    hi[0] = c.x; hi[1] = c.y; hi[2] = c.z; hi[3] = c.w;
-    hi[4] = d.x; hi[5] = d.y; hi[6] = d.z; hi[7] = d.w;
-}
+// Shared-memory counterpart of HeadSlice<__half>::load (same element layout);
+// the staged kernel below is used for fp16 storage only.
 __device__ __forceinline__ void head_from_smem(const __half *head, int j, float *lo, float *hi)
 {
     const uint4 *q = reinterpret_cast<const uint4 *>(head);
@@ -355,6 +347,7 @@ __global__ void __launch_bounds__(W * 32) qk_norm_rope_bulk(
     const int32_t *pos, int64_t rows, int nq, int nk, const __grid_constant__ FreqTable ft, float eps,
     int do_norm, unsigned *err)
 {
+    static_assert(sizeof(T) == 2, "the staged kernel serves fp16 storage");
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ __align__(16) float cs[TT][64];
     __shared__ __align__(16) float sn[TT][64];
