@@ -82,7 +82,11 @@ __device__ __forceinline__ float sq_acc(float acc, float x) { return fmaf(x, x, 
 // Packed fp32 pairs (the f32x2 instructions of sm_100): each half is one IEEE
 // round-to-nearest operation, bit-identical to __fmul_rn / __fadd_rn /
 // __fsub_rn / fmaf applied to that half alone. Operands already in adjacent
-// registers need no moves.
+// registers need no moves. Caution, measured on sm_100a with CUDA 12.9: a
+// mul2_rn whose result feeds an add2_rn / sub2_rn is contracted into one
+// packed FMA (a single rounding), despite the .rn qualifiers and with
+// --fmad=false too. Where the reference rounds the product, keep the sum
+// scalar (__fadd_rn after a packed product is not contracted).
 __device__ __forceinline__ unsigned long long f2_bits(float2 a)
 {
     unsigned long long r;

@@ -281,8 +281,8 @@ __device__ __forceinline__ void head_from_smem(const __half *head, int j, float 
 
 // Norm (optional) and rotation of one lane's 8 + 8 elements from lane-major
 // tables: w = [lo 64 | hi 64] weights, c / sn = 64 cos / sin. The products
-// and sums are those of norm_mul / rot_lo / rot_hi, two lanes of work per
-// packed f32x2 instruction, so every element is rounded as by the scalar
+// and sums are those of norm_mul / rot_lo / rot_hi, the products two elements
+// per packed f32x2 instruction, so every element is rounded as by the scalar
 // code; only the sum of squares is accumulated in four partial sums.
 __device__ __forceinline__ void norm_rotate_packed(float *xl, float *xh, int j, const float *w, const float *c,
                                                    const float *sn, bool do_norm, float eps)
@@ -323,10 +323,13 @@ __device__ __forceinline__ void norm_rotate_packed(float *xl, float *xh, int j, 
             const float2 cc = h ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
             const float2 ss = h ? make_float2(s4.z, s4.w) : make_float2(s4.x, s4.y);
             const float2 lo = make_float2(xl[e], xl[e + 1]), hi = make_float2(xh[e], xh[e + 1]);
-            const float2 yl = sub2_rn(mul2_rn(lo, cc), mul2_rn(hi, ss));  // x0*c - x1*s
-            const float2 yh = add2_rn(mul2_rn(lo, ss), mul2_rn(hi, cc));  // x0*s + x1*c
-            xl[e] = yl.x; xl[e + 1] = yl.y;
-            xh[e] = yh.x; xh[e + 1] = yh.y;
+            // Products two at a time; the sums stay scalar (a packed product
+            // feeding a packed sum is fused into one FMA by the compiler).
+            const float2 lc = mul2_rn(lo, cc), hs = mul2_rn(hi, ss), ls = mul2_rn(lo, ss), hc = mul2_rn(hi, cc);
+            xl[e] = __fsub_rn(lc.x, hs.x);  // x0*c - x1*s
+            xl[e + 1] = __fsub_rn(lc.y, hs.y);
+            xh[e] = __fadd_rn(ls.x, hc.x);  // x0*s + x1*c
+            xh[e + 1] = __fadd_rn(ls.y, hc.y);
         }
     }
 }
