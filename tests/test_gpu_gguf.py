@@ -155,3 +155,55 @@ def test_c_info_program_binds_on_the_gpu(tmp_path):
                          capture_output=True, text=True)
     assert res.returncode == 0, res.stderr
     assert res.stdout.splitlines()[-1].split() == ["bound", "2", "512", "64", "128", "16", "12"]
+
+
+@pytest.mark.parametrize("norm_type", [1, 8])
+def test_loaded_weights_drive_the_layer_ops(ds3, port, tmp_path, keep, norm_type):
+    """QK-norm+RoPE, add+RMSNorm and the router projection + top-k, each fed
+    with the tensors bound from the file (norms stored F16 or Q8_0, the router
+    F32 in layer 0 and F16 in layer 1), against the oracle on the same values."""
+    H, T, NQ, NK, HD, E, K = 512, 24, 32, 4, 128, 16, 4
+    g, raw = synthetic_model(n_layer=2, n_embd=H, n_vocab=8, norm_type=norm_type, seed=21)
+    with ds3.Gguf(g.write(tmp_path / "m.gguf")) as f:
+        w = ds3.PathWeights(f, 2)
+        try:
+            c = w.c
+
+            def wval(name, n, type_):
+                return oracle_dequant(port, type_, raw[name][0], n)
+
+            for l in range(2):
+                q, k = I.normal(30 + l, (T, NQ, HD)), I.normal(40 + l, (T, NK, HD))
+                pos = I.rng(50 + l).integers(0, 4096, T).astype(np.int32)
+                qb, kb, pb = ds3.upload(q), ds3.upload(k), ds3.upload(pos)
+                keep += [qb, kb, pb]
+                qn = ds3._Borrowed(c.attn_q_norm[l], HD * 4)
+                kn = ds3._Borrowed(c.attn_k_norm[l], HD * 4)
+                assert ds3.qk_norm_rope(qb, kb, qn, kn, pb, T, NQ, NK, HD, 1e6, 1e-6) == 0, ds3.last_error()
+                want_q, want_k = port.qk_norm_rope(q, k, wval(f"blk.{l}.attn_q_norm.weight", HD, norm_type),
+                                                   wval(f"blk.{l}.attn_k_norm.weight", HD, norm_type), pos,
+                                                   1e6, 1e-6)
+                assert_close(ds3.download(qb, np.float32, q.shape), want_q, what=f"q layer {l}")
+                assert_close(ds3.download(kb, np.float32, k.shape), want_k, what=f"k layer {l}")
+
+                x, r = I.normal(60 + l, (T, H)), I.normal(70 + l, (T, H))
+                xb, rb, sb, nb = ds3.upload(x), ds3.upload(r), ds3.empty(T * H * 4), ds3.empty(T * H * 4)
+                keep += [xb, rb, sb, nb]
+                fw = ds3._Borrowed(c.ffn_norm[l], H * 4)
+                assert ds3.add_rms_norm(xb, rb, fw, sb, nb, H, T, 1e-6) == 0, ds3.last_error()
+                want_s, want_n = port.add_rms_norm(x, r, wval(f"blk.{l}.ffn_norm.weight", H, norm_type), 1e-6)
+                assert_bitexact(ds3.download(sb, np.float32, (T, H)), want_s, f"sum layer {l}")
+                assert_close(ds3.download(nb, np.float32, (T, H)), want_n, what=f"norm layer {l}")
+
+                Wr = wval(f"blk.{l}.ffn_gate_inp.weight", E * H, l % 2).reshape(E, H)
+                lb, ib, scb = ds3.empty(T * E * 4), ds3.empty(T * K * 4), ds3.empty(T * K * 4)
+                keep += [lb, ib, scb]
+                gw = ds3._Borrowed(c.ffn_gate_inp[l], E * H * 4)
+                assert ds3.router_logits_topk(nb, gw, lb, ib, scb, T, H, E, K, True) == 0, ds3.last_error()
+                lg = port.router_logits(ds3.download(nb, np.float32, (T, H)), Wr)
+                _, want_i, want_sc = port.router(lg, K, True)
+                assert_bitexact(ds3.download(lb, np.float32, (T, E)), lg, f"router logits layer {l}")
+                assert_bitexact(ds3.download(ib, np.int32, (T, K)), want_i, f"top-k layer {l}")
+                assert_close(ds3.download(scb, np.float32, (T, K)), want_sc, what=f"scores layer {l}")
+        finally:
+            w.free()
