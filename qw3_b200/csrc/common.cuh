@@ -199,6 +199,13 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
                  : "memory");
 }
 
+// Plain arrival (release semantics: this thread's earlier shared-memory
+// writes are visible to threads that complete their wait on the phase).
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // One bulk copy global -> shared (no multicast); completion is signalled on
 // `bar` as transaction bytes. dst/src 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)

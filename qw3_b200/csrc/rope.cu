@@ -334,44 +334,46 @@ __device__ __forceinline__ void norm_rotate_packed(float *xl, float *xh, int j, 
     }
 }
 
-// head_dim = 128, large token counts: a persistent CTA streams tiles of TT
-// consecutive tokens. A tile's q rows (and its k rows) are contiguous in
-// memory, so each is one 1-D bulk async copy (TMA, no multicast) into an
-// NS-stage ring in shared memory, completing on one mbarrier per stage. The
-// bytes in flight are set by the ring (NS x tile) rather than by registers.
-// Warps then process groups of 4 heads from shared memory with the HeadSlice
-// layout and store to global memory directly. Positions of the next tile are
-// prefetched into registers, so the tile's cos/sin are ready when it lands.
-constexpr int kBulkWarps = 9;
-
-template <typename T, int TT, int NS, int W = kBulkWarps>
-__global__ void __launch_bounds__(W * 32) qk_norm_rope_bulk(
-    const T *q_src, T *q_dst, const T *k_src, T *k_dst, const float *q_w, const float *k_w,
-    const int32_t *pos, int64_t rows, int nq, int nk, const __grid_constant__ FreqTable ft, float eps,
-    int do_norm, unsigned *err)
+// fp16 storage, head_dim 128, large token counts: a persistent CTA streams
+// tiles of TT consecutive tokens through an NS-stage ring in shared memory. A
+// tile's q rows (and its k rows) are contiguous in memory, so each is one 1-D
+// bulk async copy (TMA, no multicast). The kernel is warp-specialised: warp W
+// (the producer) issues each tile's copies and computes the tile's cos/sin
+// into the stage's own table, up to NS tiles ahead; the W compute warps wait
+// on the stage's "full" mbarrier (the copies' bytes plus the producer's 32
+// arrivals after its table writes), process groups of 4 heads from shared
+// memory (HeadSlice layout, lane-major tables) straight to global memory, and
+// release the stage on its "empty" mbarrier. No CTA barrier separates the
+// tiles. All waits are bounded.
+template <int TT, int NS, int W>
+__global__ void __launch_bounds__((W + 1) * 32) qk_norm_rope_ws(
+    const __half *q_src, __half *q_dst, const __half *k_src, __half *k_dst, const float *q_w, const float *k_w,
+    const int32_t *pos, int64_t rows, int nq, int nk, const __grid_constant__ FreqTable ft, float eps, int do_norm,
+    unsigned *err)
 {
-    static_assert(sizeof(T) == 2, "the staged kernel serves fp16 storage");
+    using T = __half;
     extern __shared__ __align__(128) unsigned char ring[];
-    __shared__ __align__(16) float cs[TT][64];
-    __shared__ __align__(16) float sn[TT][64];
+    __shared__ __align__(16) float cs[NS][TT][64];
+    __shared__ __align__(16) float sn[NS][TT][64];
     __shared__ __align__(16) float wq[128];
     __shared__ __align__(16) float wk[128];
-    __shared__ __align__(8) uint64_t bars[NS];
-    constexpr int kThreads = W * 32;
-    constexpr int kPairSlots = (TT * 64 + kThreads - 1) / kThreads;
+    __shared__ __align__(8) uint64_t full[NS], empty[NS];
 
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nh = nq + nk;
     const size_t stage_elems = (size_t)TT * nh * 128;
     if (do_norm) {  // static parameters: safe to read before the wait
-        for (int i = tid; i < 256; i += W * 32) {  // lane-major halves (tab)
+        for (int i = tid; i < 256; i += (W + 1) * 32) {
             const int m = i & 127, at = (m & 64) + HeadSlice<T>::tab(m & 63);
             if (i < 128) wq[at] = q_w[m];
             else if (nk > 0) wk[at] = k_w[m];
         }
     }
     if (tid == 0) {
-        for (int s = 0; s < NS; s++) mbar_init(&bars[s], 1);
+        for (int st = 0; st < NS; st++) {
+            mbar_init(&full[st], 33);  // producer lane 0's expect_tx + 32 lanes after the cos/sin writes
+            mbar_init(&empty[st], W);
+        }
         mbar_init_fence();
     }
     __syncthreads();
@@ -381,120 +383,104 @@ __global__ void __launch_bounds__(W * 32) qk_norm_rope_bulk(
     const int64_t n_tiles = (rows + TT - 1) / TT;
     const int64_t G = gridDim.x;
     T *stage_base = reinterpret_cast<T *>(ring);
-    auto issue = [&](int s, int64_t tile) {
-        if (tid == 0) {
+    bool ok = true;
+    if (warp == W) {
+        int issued = 0;
+        for (int64_t tile = blockIdx.x; tile < n_tiles; tile += G, issued++) {
+            const int st = issued % NS;
+            if (issued >= NS && !mbar_wait(&empty[st], ((issued / NS) - 1) & 1, kWaitLimit)) {
+                ok = false;
+                break;
+            }
             const int64_t t0 = tile * TT;
             const int tok = (int)((rows - t0 < TT) ? rows - t0 : TT);
-            const uint32_t qb = (uint32_t)(tok * nq * 128 * sizeof(T));
-            const uint32_t kb = (uint32_t)(tok * nk * 128 * sizeof(T));
-            T *st = stage_base + s * stage_elems;
-            mbar_expect_tx(&bars[s], qb + kb);
-            bulk_g2s(st, q_src + t0 * nq * 128, qb, &bars[s]);
-            if (kb) bulk_g2s(st + (size_t)TT * nq * 128, k_src + t0 * nk * 128, kb, &bars[s]);
-        }
-    };
-    int64_t tile = blockIdx.x;
-    if (tile >= n_tiles) return;
-#pragma unroll
-    for (int s = 0; s < NS; s++)
-        if (tile + s * G < n_tiles) issue(s, tile + s * G);
-
-    auto load_pos = [&](int64_t tl, int32_t *pv) {
-#pragma unroll
-        for (int k = 0; k < kPairSlots; k++) {
-            const int idx = tid + k * kThreads;
-            const int64_t t = tl * TT + (idx >> 6);
-            pv[k] = (tl < n_tiles && idx < TT * 64 && t < rows) ? pos[t] : 0;
-        }
-    };
-    int32_t pcur[kPairSlots], pnxt[kPairSlots];
-    load_pos(tile, pcur);
-
-    const int lane = tid & 31, warp = tid >> 5, sub = lane >> 3, j = lane & 7;
-    uint32_t parity = 0;
-    for (int it = 0; tile < n_tiles; tile += G, it++) {
-        const int s = it % NS;
-        load_pos(tile + G, pnxt);
-#pragma unroll
-        for (int k = 0; k < kPairSlots; k++) {
-            const int idx = tid + k * kThreads;
-            if (idx < TT * 64) {
-                float sv, cv;
-                sincosf(__fmul_rn((float)pcur[k], ft.f[idx & 63]), &sv, &cv);
-                cs[idx >> 6][HeadSlice<T>::tab(idx & 63)] = cv;
-                sn[idx >> 6][HeadSlice<T>::tab(idx & 63)] = sv;
+            if (lane == 0) {
+                const uint32_t qb = (uint32_t)(tok * nq * 128 * sizeof(T));
+                const uint32_t kb = (uint32_t)(tok * nk * 128 * sizeof(T));
+                T *dst = stage_base + st * stage_elems;
+                mbar_expect_tx(&full[st], qb + kb);
+                bulk_g2s(dst, q_src + t0 * nq * 128, qb, &full[st]);
+                if (kb) bulk_g2s(dst + (size_t)TT * nq * 128, k_src + t0 * nk * 128, kb, &full[st]);
             }
-        }
-        const bool ok = __syncthreads_and(mbar_wait(&bars[s], (parity >> s) & 1u, kWaitLimit));
-        parity ^= 1u << s;
-        if (!ok) {
-            // Record the timeout, let this CTA's copies land (bounded), stop.
-            if (tid == 0) {
-                flag_error(err, kErrWaitTimeout);
-                for (int k = 0; k < NS; k++) {
-                    const int ss = (s + k) % NS;
-                    if (tile + k * G < n_tiles)
-                        mbar_wait(&bars[ss], ((parity >> ss) & 1u) ^ (k == 0 ? 1u : 0u), kWaitLimit);
+#pragma unroll
+            for (int tl = 0; tl < TT; tl++) {
+                const float pf = tl < tok ? (float)pos[t0 + tl] : 0.0f;
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int pr = lane + 32 * h;
+                    float sv = 0.0f, cv = 1.0f;
+                    if (tl < tok) sincosf(__fmul_rn(pf, ft.f[pr]), &sv, &cv);
+                    cs[st][tl][HeadSlice<T>::tab(pr)] = cv;
+                    sn[st][tl][HeadSlice<T>::tab(pr)] = sv;
                 }
             }
-            return;
+            mbar_arrive(&full[st]);  // release: the table writes are visible to the waiting warps
         }
-        const int64_t t0 = tile * TT;
-        const int tok = (int)((rows - t0 < TT) ? rows - t0 : TT);
-        const T *sq = stage_base + s * stage_elems;
-        const T *sk = sq + (size_t)TT * nq * 128;
-        const int n_heads = tok * nh;
-        const int n_groups = (n_heads + 3) >> 2;
-        for (int g = warp; g < n_groups; g += W) {
-            const int h = 4 * g + sub;
-            const bool act = h < n_heads;
-            const int hc = act ? h : 0;
-            // token within the tile: no integer division for 1- and 2-token tiles
-            const int tl = TT == 1 ? 0 : TT == 2 ? (hc >= nh ? 1 : 0) : hc / nh, hh = hc - tl * nh;
-            const bool is_k = hh >= nq;
-            const T *src = is_k ? sk + (size_t)(tl * nk + (hh - nq)) * 128 : sq + (size_t)(tl * nq + hh) * 128;
-            float xl[8], xh[8];
-            head_from_smem(src, j, xl, xh);
-            norm_rotate_packed(xl, xh, j, is_k ? wk : wq, cs[tl], sn[tl], do_norm, eps);
-            if (act) {
-                const int64_t t = t0 + tl;
-                T *dst = is_k ? k_dst + (t * nk + (hh - nq)) * 128 : q_dst + (t * nq + hh) * 128;
-                HeadSlice<T>::store(dst, j, xl, xh);
+        // Do not leave with copies in flight: the last stages issued must land.
+        for (int k = issued - 1; k >= 0 && k >= issued - NS; k--)
+            if (!mbar_wait(&full[k % NS], (k / NS) & 1, kWaitLimit)) ok = false;
+    } else {
+        const int sub = lane >> 3, j = lane & 7;
+        int it = 0;
+        for (int64_t tile = blockIdx.x; tile < n_tiles; tile += G, it++) {
+            const int st = it % NS;
+            if (!mbar_wait(&full[st], (it / NS) & 1, kWaitLimit)) {
+                ok = false;
+                break;
             }
+            const int64_t t0 = tile * TT;
+            const int tok = (int)((rows - t0 < TT) ? rows - t0 : TT);
+            const T *sq = stage_base + st * stage_elems;
+            const T *sk = sq + (size_t)TT * nq * 128;
+            const int n_heads = tok * nh;
+            const int n_groups = (n_heads + 3) >> 2;
+            for (int g = warp; g < n_groups; g += W) {
+                const int h = 4 * g + sub;
+                const bool act = h < n_heads;
+                const int hc = act ? h : 0;
+                const int tl = TT == 1 ? 0 : TT == 2 ? (hc >= nh ? 1 : 0) : hc / nh, hh = hc - tl * nh;
+                const bool is_k = hh >= nq;
+                const T *src = is_k ? sk + (size_t)(tl * nk + (hh - nq)) * 128 : sq + (size_t)(tl * nq + hh) * 128;
+                float xl[8], xh[8];
+                head_from_smem(src, j, xl, xh);
+                norm_rotate_packed(xl, xh, j, is_k ? wk : wq, cs[st][tl], sn[st][tl], do_norm, eps);
+                if (act) {
+                    const int64_t t = t0 + tl;
+                    T *dst = is_k ? k_dst + (t * nk + (hh - nq)) * 128 : q_dst + (t * nq + hh) * 128;
+                    HeadSlice<T>::store(dst, j, xl, xh);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
         }
-        __syncthreads();  // stage s and cs/sn are free
-        if (tile + NS * G < n_tiles) issue(s, tile + NS * G);
-#pragma unroll
-        for (int k = 0; k < kPairSlots; k++) pcur[k] = pnxt[k];
     }
+    if (!ok && lane == 0) flag_error(err, kErrWaitTimeout);
 }
 
-template <typename T, int TT, int NS, int W = kBulkWarps>
-cudaError_t run_bulk(const LaunchCtx &c, const void *qs, void *qd, const void *ks, void *kd, const float *q_w,
-                     const float *k_w, const int32_t *pos, int64_t rows, int nq, int nk, const FreqTable &ft,
-                     float eps, int do_norm)
+template <int TT, int NS, int W>
+cudaError_t run_ws(const LaunchCtx &c, const void *qs, void *qd, const void *ks, void *kd, const float *q_w,
+                   const float *k_w, const int32_t *pos, int64_t rows, int nq, int nk, const FreqTable &ft, float eps,
+                   int do_norm)
 {
-    const size_t smem = (size_t)NS * TT * (nq + nk) * 128 * sizeof(T);
+    auto kern = qk_norm_rope_ws<TT, NS, W>;
+    const size_t smem = (size_t)NS * TT * (nq + nk) * 128 * sizeof(__half);
     static size_t configured = 0;
     if (smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(qk_norm_rope_bulk<T, TT, NS, W>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         configured = smem;
-        // Its occupancy needs most of the shared memory (0.73 vs 0.64 of the
-        // copy peak at T=32768 under the common 50 % carveout).
-        keep_driver_carveout(reinterpret_cast<const void *>(qk_norm_rope_bulk<T, TT, NS, W>));
+        keep_driver_carveout(reinterpret_cast<const void *>(kern));
     }
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_bulk<T, TT, NS, W>, W * 32, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (W + 1) * 32, smem);
     if (per_sm < 1) per_sm = 1;
     const int64_t tiles = (rows + TT - 1) / TT;
     const int64_t cap = (int64_t)c.n_sm * per_sm;
-    launch_ks(c, qk_norm_rope_bulk<T, TT, NS, W>, dim3((unsigned)(tiles < cap ? tiles : cap)), dim3(W * 32),
-              smem, (const T *)qs, (T *)qd, (const T *)ks, (T *)kd, q_w, k_w, pos, rows, nq, nk, ft, eps, do_norm,
-              c.err);
+    launch_ks(c, kern, dim3((unsigned)(tiles < cap ? tiles : cap)), dim3((W + 1) * 32), smem, (const __half *)qs,
+              (__half *)qd, (const __half *)ks, (__half *)kd, q_w, k_w, pos, rows, nq, nk, ft, eps, do_norm, c.err);
     return cudaGetLastError();
 }
+
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
@@ -613,15 +599,16 @@ cudaError_t launch_qk_norm_rope(const LaunchCtx &c, const void *q_src, void *q_d
     const int groups = (kTileTok * (nq + nk) + 3) / 4;
     const int use_hd = (hd == 128 && (data & m) == 0 && groups <= kTileWarps * 2) ? 128 : 0;
     (void)wts;
-    // fp16 storage at large token counts: the TMA-staged kernel (measured at
-    // T=32768: 126 us vs 138 us for the register-tile kernel; fp32 is faster
-    // with the register-tile kernel, 176 us vs 203 us). 2-token tiles, 3
-    // stages, 9 warps measured best against 18 or 12 warps and 4-token tiles.
+    // fp16 storage at large token counts: the warp-specialised staged kernel
+    // (T=32768: 98.5 us, against 109 us for a staged kernel with two CTA
+    // barriers per tile and 180 us for the register-tile kernel; fp32 is
+    // faster with the register-tile kernel). 2-token tiles, 3 stages, 9
+    // compute warps measured best against 2 or 4 stages, 6 or 12 warps, and
+    // 1- or 4-token tiles.
     if (use_hd && storage && rows >= 2048) {
         const uintptr_t al = reinterpret_cast<uintptr_t>(q_src) | reinterpret_cast<uintptr_t>(k_src);
         if ((al & 15u) == 0) {
-            return run_bulk<__half, 2, 3>(c, q_src, q_dst, k_src, k_dst, q_w, k_w, pos, rows, nq, nk, ft, eps,
-                                          do_norm);
+            return run_ws<2, 3, 9>(c, q_src, q_dst, k_src, k_dst, q_w, k_w, pos, rows, nq, nk, ft, eps, do_norm);
         }
     }
     if (storage)

@@ -91,10 +91,6 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t *bar)
 {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
-{
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
 
 // tpc = tokens per cluster (<= NW * TPW), chosen by the host so that the
 // clusters fill the GPU in one wave.
