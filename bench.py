@@ -342,6 +342,10 @@ def main():
     ap.add_argument("--profile", action="store_true", help="short run for ncu: no e2e, baseline or configs")
     ap.add_argument("--rope-f16", type=int, default=0, metavar="T",
                     help="time only QK-norm+RoPE with fp16 storage on T tokens (a small case for ncu)")
+    ap.add_argument("--router-proj", type=int, default=0, metavar="T",
+                    help="time only the router projection + top-8 on T tokens (a small case for ncu)")
+    ap.add_argument("--expert-lists", type=int, default=0, metavar="T",
+                    help="time only the device per-expert token lists for T tokens (a small case for ncu)")
     ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between ops (1/0)")
     args = ap.parse_args()
     rank, world, local = dist_env()
@@ -385,8 +389,13 @@ def main():
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
-    if args.rope_f16:
-        line = run_rope_f16(ds3, args.rope_f16, max_over_ranks, barrier)
+    if args.rope_f16 or args.router_proj or args.expert_lists:
+        if args.rope_f16:
+            line = run_rope_f16(ds3, args.rope_f16, max_over_ranks, barrier)
+        elif args.router_proj:
+            line = run_router_proj(ds3, args.router_proj, max_over_ranks, barrier)
+        else:
+            line = run_expert_lists(ds3, args.expert_lists, max_over_ranks, barrier)
         if rank == 0:
             emit(line)
         return 0
@@ -716,6 +725,32 @@ def run_rope_f16(ds3, T, max_over_ranks, barrier):
         b.free()
     return {"workload": f"qk_norm_rope_f16_T{T}", "us": round(ms * 1e3, 3), "algo_bytes": nbytes,
             "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1), "frac_of_measured_peak": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)}
+
+
+def run_router_proj(ds3, T, max_over_ranks, barrier):
+    """Router projection [T, 2048] x [128, 2048] fused with softmax/top-8,
+    bit-exact sequential fp32 sums (ds3_cuda_router_logits_topk)."""
+    x, w = ds3.upload(I.normal(7300, (T, H))), ds3.upload(I.normal(7301, (E, H), 0.0, 0.05))
+    ix, sc = ds3.empty(T * K * 4), ds3.empty(T * K * 4)
+    fns = [lambda: ds3.router_logits_topk(x, w, None, ix, sc, T, H, E, K, True)]
+    ms = time_launches(ds3, fns, 20, max_over_ranks, barrier)
+    for b in (x, w, ix, sc):
+        b.free()
+    return {"workload": f"router_logits_topk_T{T}", "us": round(ms * 1e3, 3),
+            "gflops": round(2 * T * E * H / (ms * 1e-3) / 1e9, 1)}
+
+
+def run_expert_lists(ds3, T, max_over_ranks, barrier):
+    """Device per-expert token lists for T tokens x top-8 (ds3_cuda_moe_expert_lists)."""
+    lg = ds3.upload(I.normal(7400, (T, E), 0.0, 2.0))
+    ix, sc = ds3.empty(T * K * 4), ds3.empty(T * K * 4)
+    ds3.router_softmax_topk(lg, None, ix, sc, T, E, K, True)
+    cnt, ids, gsc, slot = ds3.empty(E * 4), ds3.empty(E * T * 4), ds3.empty(E * T * 4), ds3.empty(T * K * 4)
+    fns = [lambda: ds3.moe_expert_lists(ix, sc, cnt, ids, gsc, slot, T, E, K, T)]
+    ms = time_launches(ds3, fns, 20, max_over_ranks, barrier)
+    for b in (lg, ix, sc, cnt, ids, gsc, slot):
+        b.free()
+    return {"workload": f"moe_expert_lists_T{T}", "us": round(ms * 1e3, 3)}
 
 
 def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k):
