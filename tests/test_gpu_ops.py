@@ -218,7 +218,7 @@ def test_qk_norm_rope_shapes(ds3, B, port, nq, nk, hd):
         assert_close(f32(kb, ds3, k.shape), ko, what="k")
 
 
-@pytest.mark.parametrize("T", [128, 2049])
+@pytest.mark.parametrize("T", [128, 2049, 4100])
 def test_qk_norm_rope_fp16_storage(ds3, B, port, T):
     q = I.normal(7, (T, 32, 128)).astype(np.float16)
     k = I.normal(8, (T, 4, 128)).astype(np.float16)
