@@ -270,7 +270,9 @@ int ds3_cuda_router_softmax_topk(const ds3_cuda_buffer_t *logits,
  * (cap = n_tokens there). slot_of int32 [n_tokens * n_used] (or NULL) gets
  * ex*cap + j for each (token, slot): pass it as y_rows to
  * moe_combine_residual to read expert outputs in this layout. Slots past
- * counts[ex] are not written. n_expert <= 256. */
+ * counts[ex] are not written. counts[ex] is clamped to cap; a list that
+ * would overflow, or an expert id outside [0, n_expert), makes the call
+ * return -1 and leaves -1 in the affected slot_of entries. n_expert <= 256. */
 int ds3_cuda_moe_expert_lists(const ds3_cuda_buffer_t *idx, const ds3_cuda_buffer_t *scores,
                               ds3_cuda_buffer_t *counts, ds3_cuda_buffer_t *ids,
                               ds3_cuda_buffer_t *gscores, ds3_cuda_buffer_t *slot_of,
@@ -301,7 +303,9 @@ int ds3_cuda_swiglu(const ds3_cuda_buffer_t *gate, const ds3_cuda_buffer_t *up,
  * scatter_add_weighted + vec_add (src/ds3_engine.c:1012-1019):
  * out[t] = residual[t] + sum_k w[t,k] * y[row(t,k)], accumulated from zero in
  * k order. row(t,k) = y_rows[t*n_used+k] (int32), or t*n_used+k when y_rows
- * is NULL. out may alias residual. */
+ * is NULL. out may alias residual. A mapped row outside y (a -1 left by
+ * moe_expert_lists, or an index past y's last row) counts as a zero row and
+ * makes the call return -1; y is never read outside its buffer. */
 int ds3_cuda_moe_combine_residual(const ds3_cuda_buffer_t *y, const ds3_cuda_buffer_t *y_rows,
                                   const ds3_cuda_buffer_t *w, const ds3_cuda_buffer_t *residual,
                                   ds3_cuda_buffer_t *out,
@@ -342,6 +346,11 @@ const char *ds3_cuda_last_error(void);
  * wait ran out and was reported through the device error word (the word is
  * consumed), -1 otherwise. No fault, trap or hang is involved. */
 int ds3_cuda_selftest_bounded_wait(uint32_t polls);
+
+/* new: the compute capability the library's kernels were compiled for, as
+ * the CUDA runtime reports it for a loaded kernel (major*10 + minor; 100 for
+ * sm_100a code), or -1 without a usable device. Needs ds3_cuda_init. */
+int ds3_cuda_kernel_binary_version(void);
 
 /* Reads and clears the device error word (bit 0: bad token id; bit 1: a
  * bounded wait ran out). Synchronises the module stream. */

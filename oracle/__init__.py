@@ -54,11 +54,21 @@ _PORT_ONLY = {
 }
 
 
+def reference_dir() -> str:
+    """The reference checkout the Makefile builds from: DS3_REFERENCE_DIR if
+    set, else the Makefile's default REF (a sibling of the repository)."""
+    env = os.environ.get("DS3_REFERENCE_DIR")
+    if env:
+        return env
+    out = subprocess.run(["make", "-s", "-C", str(HERE), "print-ref"], capture_output=True, text=True)
+    return out.stdout.strip()
+
+
 def build(ref_dir: str | None = None, quiet: bool = True) -> None:
     """Compile the oracles with oracle/Makefile (the reference leg only when
     the reference tree is present)."""
     targets = ["oracle"]
-    ref = ref_dir or os.environ.get("DS3_REFERENCE_DIR", "/root/reference")
+    ref = ref_dir or reference_dir()
     if Path(ref, "src", "ds3_reference.c").exists():
         targets.append("ref")
     subprocess.run(["make", "-s", "-C", str(HERE), f"REF={ref}", *targets], check=True,

@@ -985,7 +985,7 @@ int ds3_cuda_moe_combine_residual(const ds3_cuda_buffer_t *y, const ds3_cuda_buf
     return finish(op,
                   ds3::launch_combine(ctx(), (const float *)dptr(y), (const int32_t *)dptr(y_rows),
                                       (const float *)dptr(w), (const float *)dptr(residual), (float *)dptr(out),
-                                      n_tokens, (int)n_used, n_cols),
+                                      n_tokens, (int)n_used, n_cols, (int64_t)(y->bytes / ((size_t)n_cols * 4))),
                   ps);
 }
 
@@ -1099,6 +1099,12 @@ int ds3_cuda_selftest_bounded_wait(uint32_t polls)
 }
 
 const char *ds3_cuda_last_error(void) { return g_last_error.c_str(); }
+
+int ds3_cuda_kernel_binary_version(void)
+{
+    if (!ready("kernel_binary_version")) return -1;
+    return ds3::kernel_binary_version();
+}
 
 
 uint32_t ds3_cuda_device_errors(void)

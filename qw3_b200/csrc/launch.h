@@ -93,6 +93,8 @@ cudaError_t launch_moe_expert_lists(const LaunchCtx &c, const int32_t *idx, cons
                                     int n_expert, int64_t cap);
 
 cudaError_t launch_bounded_wait_selftest(const LaunchCtx &c, uint32_t polls);
+// Compute capability (major*10 + minor) of the loaded kernel code, or -1.
+int kernel_binary_version();
 
 // Router projection (sequential fp32 dot products, reference order) + top-k.
 bool router_gemv_fast(int64_t n_tokens, int n_embd, int n_expert, int n_used, const void *x, const void *W);
@@ -109,7 +111,7 @@ cudaError_t launch_swiglu(const LaunchCtx &c, const float *gate, const float *up
 
 cudaError_t launch_combine(const LaunchCtx &c, const float *y, const int32_t *y_rows,
                            const float *w, const float *residual, float *out, int64_t n_tokens,
-                           int n_used, int64_t n_cols);
+                           int n_used, int64_t n_cols, int64_t n_y_rows);
 
 cudaError_t launch_vec_add(const LaunchCtx &c, const float *a, const float *b, float *out,
                            int64_t n);

@@ -118,11 +118,21 @@ __global__ void swiglu_scalar(const float *gate, const float *up, const float *r
 // --------------------------------------------------------- combine + residual
 // One thread per (token, float4 column): all n_used expert rows of that
 // column are loaded before the sum, which runs from zero in k order.
+// A mapped row outside [0, n_y_rows) (a -1 from moe_expert_lists for a bad
+// expert id or a full list) reads as a zero row and sets the bad-id bit of
+// the error word; y is never read out of bounds.
+__device__ __forceinline__ bool row_ok(int64_t r, int64_t n_y_rows, unsigned *err, bool report)
+{
+    if (r >= 0 && r < n_y_rows) return true;
+    if (report) flag_error(err, kErrBadId);
+    return false;
+}
+
 template <int K>
 __global__ void __launch_bounds__(128) combine_vec(const float4 *y, const int32_t *y_rows,
                                                    const float *w, const float4 *residual,
                                                    float4 *out, int64_t n_tokens, int n_used,
-                                                   int64_t cols4)
+                                                   int64_t cols4, int64_t n_y_rows, unsigned *err)
 {
     pdl_wait();
     pdl_trigger();
@@ -139,7 +149,7 @@ __global__ void __launch_bounds__(128) combine_vec(const float4 *y, const int32_
 #pragma unroll
         for (int k = 0; k < K; k++) {
             const int64_t r = y_rows ? (int64_t)y_rows[t * K + k] : t * K + k;
-            yv[k] = ld_stream(y + r * cols4 + c);
+            yv[k] = row_ok(r, n_y_rows, err, c == 0) ? ld_stream(y + r * cols4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
             wk[k] = __ldg(w + t * K + k);
         }
 #pragma unroll
@@ -152,7 +162,8 @@ __global__ void __launch_bounds__(128) combine_vec(const float4 *y, const int32_
     } else {
         for (int k = 0; k < nk; k++) {
             const int64_t r = y_rows ? (int64_t)y_rows[t * nk + k] : t * nk + k;
-            const float4 yv = ld_stream(y + r * cols4 + c);
+            const float4 yv =
+                row_ok(r, n_y_rows, err, c == 0) ? ld_stream(y + r * cols4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
             const float wk = __ldg(w + t * nk + k);
             acc.x = __fadd_rn(acc.x, __fmul_rn(wk, yv.x));
             acc.y = __fadd_rn(acc.y, __fmul_rn(wk, yv.y));
@@ -195,7 +206,7 @@ __global__ void __launch_bounds__(128) combine8_tokmajor(const float4 *y, const 
 
 __global__ void combine_scalar(const float *y, const int32_t *y_rows, const float *w,
                                const float *residual, float *out, int64_t n_tokens, int n_used,
-                               int64_t cols)
+                               int64_t cols, int64_t n_y_rows, unsigned *err)
 {
     pdl_wait();
     pdl_trigger();
@@ -205,7 +216,8 @@ __global__ void combine_scalar(const float *y, const int32_t *y_rows, const floa
         float acc = 0.0f;
         for (int k = 0; k < n_used; k++) {
             const int64_t r = y_rows ? (int64_t)y_rows[t * n_used + k] : t * n_used + k;
-            acc = __fadd_rn(acc, __fmul_rn(w[t * n_used + k], y[r * cols + c]));
+            const float yv = row_ok(r, n_y_rows, err, c == 0) ? y[r * cols + c] : 0.0f;
+            acc = __fadd_rn(acc, __fmul_rn(w[t * n_used + k], yv));
         }
         out[e] = __fadd_rn(residual[e], acc);
     }
@@ -329,7 +341,7 @@ cudaError_t launch_swiglu(const LaunchCtx &c, const float *gate, const float *up
 
 cudaError_t launch_combine(const LaunchCtx &c, const float *y, const int32_t *y_rows,
                            const float *w, const float *residual, float *out, int64_t n_tokens,
-                           int n_used, int64_t n_cols)
+                           int n_used, int64_t n_cols, int64_t n_y_rows)
 {
     if (n_tokens <= 0 || n_cols <= 0) return cudaSuccess;
     if (n_cols % 4 == 0 && al16(y) && al16(residual) && al16(out)) {
@@ -345,12 +357,14 @@ cudaError_t launch_combine(const LaunchCtx &c, const float *y, const int32_t *y_
             return cudaGetLastError();
         }
         if (n_used == 8)
-            launch_k(c, combine_vec<8>, dim3(blocks), dim3(128), y4, y_rows, w, r4, o4, n_tokens, n_used, cols4);
+            launch_k(c, combine_vec<8>, dim3(blocks), dim3(128), y4, y_rows, w, r4, o4, n_tokens, n_used, cols4,
+                     n_y_rows, c.err);
         else
-            launch_k(c, combine_vec<0>, dim3(blocks), dim3(128), y4, y_rows, w, r4, o4, n_tokens, n_used, cols4);
+            launch_k(c, combine_vec<0>, dim3(blocks), dim3(128), y4, y_rows, w, r4, o4, n_tokens, n_used, cols4,
+                     n_y_rows, c.err);
     } else {
         launch_k(c, combine_scalar, dim3(grid_for(c, n_tokens * n_cols, 256, 16)), dim3(256), 
-            y, y_rows, w, residual, out, n_tokens, n_used, n_cols);
+            y, y_rows, w, residual, out, n_tokens, n_used, n_cols, n_y_rows, c.err);
     }
     return cudaGetLastError();
 }

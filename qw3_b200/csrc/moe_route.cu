@@ -99,7 +99,9 @@ __global__ void __launch_bounds__(kRouteThreads) moe_expert_lists_k(
         base += total;
         __syncthreads();  // wpre / total are rewritten by the next pass
     }
-    if (tid == 0) counts[ex] = (int32_t)base;
+    // Clamped to the list capacity: a consumer looping j < counts[ex] stays
+    // inside this expert's list (an overflow is already flagged above).
+    if (tid == 0) counts[ex] = (int32_t)(base < cap ? base : cap);
 }
 
 // Self-test of the bounded mbarrier wait: the barrier expects one arrival
@@ -117,6 +119,16 @@ __global__ void bounded_wait_selftest_k(uint32_t polls, unsigned *err)
 }
 
 }  // namespace
+
+int kernel_binary_version()
+{
+    cudaFuncAttributes a;
+    if (cudaFuncGetAttributes(&a, bounded_wait_selftest_k) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    return a.binaryVersion;
+}
 
 cudaError_t launch_bounded_wait_selftest(const LaunchCtx &c, uint32_t polls)
 {

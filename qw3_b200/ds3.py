@@ -89,6 +89,7 @@ _SIGS = {
     "last_error": (C.c_char_p, []),
     "device_errors": (_U32, []),
     "selftest_bounded_wait": (_I, [_U32]),
+    "kernel_binary_version": (_I, []),
     "dequantize_f32": (_I, [_P, _I, _U64, _P]),
     # include/ds3_cuda_gguf.h
     "gguf_open": (_P, [C.c_char_p]),
@@ -407,6 +408,10 @@ def timer_elapsed_ms(a: int, b: int) -> float:
 
 def device_errors() -> int:
     return lib().ds3_cuda_device_errors()
+
+
+def kernel_binary_version() -> int:
+    return lib().ds3_cuda_kernel_binary_version()
 
 
 def selftest_bounded_wait(polls: int = 1000) -> int:

@@ -38,13 +38,11 @@ def test_python_mirror_covers_the_header(lib):
     assert declared == set(ds3._SIGS), declared ^ set(ds3._SIGS)
 
 
-def test_only_sm100a_code_is_embedded():
-    out = subprocess.run(["/usr/local/cuda/bin/cuobjdump", "--list-elf", str(ds3.LIB_PATH)],
-                         capture_output=True, text=True)
-    if out.returncode != 0:
-        pytest.skip("cuobjdump unavailable")
-    arches = {l.split(".")[-2] for l in out.stdout.splitlines() if ".sm_" in l}
-    assert arches == {"sm_100a"}, arches
+def test_build_targets_only_sm100a():
+    # The build asks nvcc for sm_100a machine code and nothing else (no PTX
+    # for JIT, no other architecture); the GPU suite checks the loaded
+    # kernels' binary version at run time.
+    assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
 def test_calls_before_init_fail_cleanly(lib):

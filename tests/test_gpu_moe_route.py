@@ -86,3 +86,45 @@ def test_gathered_flow_equals_token_major_combine(ds3, up, port):
     assert ds3.moe_combine_residual(up(y_tok), None, up(sc), up(r), o2, T, K, H) == 0
     assert_bitexact(ds3.download(o1, np.float32, (T, H)), ds3.download(o2, np.float32, (T, H)), "combine")
     assert_bitexact(ds3.download(o2, np.float32, (T, H)), port.combine(y_tok, sc, r), "oracle")
+
+
+def test_combine_row_map_out_of_range(ds3, up, port):
+    """A row map holding -1 (what moe_expert_lists leaves for a bad id or a
+    full list) or an index past y's last row: those rows count as zero, y is
+    never read outside its buffer, and the call returns -1."""
+    T, K, H = 6, 8, 256
+    n_y = T * K
+    y = I.normal(21, (n_y, H))
+    w = I.rng(22).uniform(0, 1, (T, K)).astype(np.float32)
+    r = I.normal(23, (T, H))
+    rows = I.rng(24).permutation(n_y).astype(np.int32).reshape(T, K)
+    rows[1, 3] = -1
+    rows[4, 0] = n_y
+    rows[5, 7] = 1 << 30
+    o = up(np.zeros((T, H), np.float32))
+    assert ds3.moe_combine_residual(up(y), up(rows), up(w), up(r), o, T, K, H) == -1
+    # Expected: the bad entries read an all-zero row appended to y.
+    y_ext = np.concatenate([y, np.zeros((1, H), np.float32)])
+    fixed = np.where((rows < 0) | (rows >= n_y), n_y, rows).astype(np.int32)
+    assert_bitexact(ds3.download(o, np.float32, (T, H)), port.combine(y_ext, w, r, fixed.reshape(-1)), "zero rows")
+    # The error word was consumed by the failing call; a good call succeeds.
+    assert ds3.moe_combine_residual(up(y), up(fixed % n_y), up(w), up(r), o, T, K, H) == 0
+
+
+def test_expert_lists_counts_clamped_to_cap(ds3, up, port):
+    """A list that overflows its capacity: counts[ex] stays <= cap, the
+    overflowing slots get -1 and the call returns -1."""
+    T, E, K, cap = 8, 16, 2, 4
+    idx = np.tile(np.array([[3, 5]], np.int32), (T, 1))  # expert 3 and 5 chosen by all 8 tokens
+    sc = np.full((T, K), 0.5, np.float32)
+    cb, ib, gb, sb = (up(np.zeros(E, np.int32)), up(np.zeros(E * cap, np.int32)), up(np.zeros(E * cap, np.float32)),
+                      up(np.zeros(T * K, np.int32)))
+    assert ds3.moe_expert_lists(up(idx), up(sc), cb, ib, gb, sb, T, E, K, cap) == -1
+    counts = ds3.download(cb, np.int32, (E,))
+    assert counts[3] == cap and counts[5] == cap and counts.max() == cap
+    slot = ds3.download(sb, np.int32, (T, K))
+    assert (slot[:cap, 0] == 3 * cap + np.arange(cap)).all() and (slot[cap:, :] == -1).all()
+    rc, want_counts, _, _, want_slot = oracle.moe_expert_lists(port, idx, sc, E, cap)
+    assert rc == -1
+    assert_bitexact(counts, want_counts, "counts")
+    assert_bitexact(slot.reshape(-1), want_slot, "slot_of")

@@ -233,6 +233,24 @@ def test_qk_norm_rope_fp16_storage(ds3, B, port, T):
     assert_close(got_k, ko, rtol=2e-3, atol=1e-3, what="k fp16")
 
 
+@pytest.mark.parametrize("T,nq,nk", [(2048, 32, 0), (3001, 16, 2), (2050, 5, 3)])
+def test_qk_norm_rope_fp16_staged_head_splits(ds3, B, port, T, nq, nk):
+    """The warp-specialised fp16 kernel (>= 2048 tokens) with no K heads and
+    with other Q/K head splits, including an odd token count (ragged last tile)."""
+    q = I.normal(17, (T, nq, 128)).astype(np.float16)
+    k = I.normal(18, (T, max(nk, 1), 128))[:, :nk].astype(np.float16)
+    qw, kw = I.gamma(128, 19), I.gamma(128, 20)
+    pos = (np.arange(T, dtype=np.int32) * 7919) % 32768
+    qb = B.up(q)
+    kb = B.up(k) if nk else None
+    assert ds3.qk_norm_rope(qb, kb, B.up(qw), B.up(kw), B.up(pos), T, nq, nk, 128, 1e6, 1e-6, F16) == 0
+    qo, ko = port.qk_norm_rope(q.astype(np.float32), k.astype(np.float32), qw, kw, pos, 1e6, 1e-6)
+    assert_close(ds3.download(qb, np.float16, q.shape).astype(np.float32), qo, rtol=2e-3, atol=1e-3, what="q fp16")
+    if nk:
+        assert_close(ds3.download(kb, np.float16, k.shape).astype(np.float32), ko, rtol=2e-3, atol=1e-3,
+                     what="k fp16")
+
+
 def test_rope_standalone(ds3, B, port):
     g = load_golden("qk_norm_rope.npz")
     T = g["q"].shape[0]
@@ -428,6 +446,11 @@ def test_argument_errors(ds3, B):
             ds3.buffer_view(x, 1024, 2048)  # past the end: NULL
     finally:
         v.free()
+
+
+def test_kernels_are_sm100_code(ds3):
+    # What the CUDA runtime reports for a kernel it loaded from the library.
+    assert ds3.kernel_binary_version() == 100
 
 
 def test_bounded_wait_gives_up_and_reports(ds3):
