@@ -250,7 +250,33 @@ constexpr uint32_t kWaitLimit = 1u << 22;
 // parameters (norm weights, embedding table, frequency table) may be read
 // before pdl_wait. Without the PDL launch attribute both are no-ops.
 // ------------------------------------------------------------------------
+// ------------------------------------------------------------------------
+// L2 prefetch ahead of pdl_wait. A kernel whose CTAs are already resident
+// while the previous grid runs (PDL) asks the L2 for the activation bytes it
+// is about to read (cp.async.bulk.prefetch.L2: a hint, no data returned), so
+// the DRAM round trip overlaps the previous kernel instead of following it.
+// This is safe for any input, including one the previous grid writes: every
+// global store lands in the L2, the device's point of coherence, so a load
+// issued after pdl_wait sees the final data whatever was prefetched before.
+// (Loads made before the wait to steer a prefetch must bypass L1 — ld.cg —
+// since L1 is not coherent with the other SMs' stores.) Only the part of
+// [p, p + bytes) that lies on whole 16-byte units is prefetched, so nothing
+// outside the range is touched.
+// ------------------------------------------------------------------------
+__device__ __forceinline__ void prefetch_l2(const void *p, uint64_t bytes)
+{
+    uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uintptr_t end = (a + bytes) & ~(uintptr_t)15;
+    a = (a + 15) & ~(uintptr_t)15;
+    while (a < end) {
+        const uint32_t n = (uint32_t)((end - a) < 65536u ? (end - a) : 65536u);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
+        a += n;
+    }
+}
+
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 
 }  // namespace ds3

@@ -192,8 +192,6 @@ struct EmbedArgs {
 template <int TYPE, int NB, bool NORM>
 __global__ void __launch_bounds__(kWarps * 32) embed_warp(const EmbedArgs a)
 {
-    pdl_wait();
-    pdl_trigger();
     constexpr int kRowBytes = NB * BlockBytes<TYPE>::v;
     constexpr int kSlot = (kRowBytes + 15) & ~15;
     __shared__ __align__(128) uint8_t slots[kWarps][2][kSlot];
@@ -204,6 +202,15 @@ __global__ void __launch_bounds__(kWarps * 32) embed_warp(const EmbedArgs a)
     const int warps = blockDim.x >> 5;  // <= kWarps
     const int64_t stride = (int64_t)gridDim.x * warps;
     int64_t cur = (int64_t)blockIdx.x * warps + wid;
+    // While the previous kernel runs: read this warp's first id past L1 and
+    // prefetch that table row into L2 (a hint only: the id is read again
+    // after the wait, and a stale or bad id just prefetches nothing useful).
+    if (cur < a.n_ids && lane == 0) {
+        const int32_t hint = __ldcg(a.ids + cur);
+        if (hint >= 0 && hint < a.n_vocab) prefetch_l2(a.table + (uint64_t)hint * a.row_stride, kRowBytes);
+    }
+    pdl_wait();
+    pdl_trigger();
     if (cur >= a.n_ids) return;  // whole warp leaves together; no CTA barrier below
 
     if (!a.use_bulk) {

@@ -71,6 +71,11 @@ template <int U>
 __global__ void __launch_bounds__(256) swiglu_blk(const float4 *gate, const float4 *up, const float *row_w,
                                                   float4 *out, uint32_t units, uint32_t cols4)
 {
+    if (threadIdx.x < 2) {  // this CTA's gate / up ranges, into L2 while the previous kernel runs
+        const uint32_t u0 = blockIdx.x * (256u * U);
+        const uint32_t n = units - u0 < 256u * U ? units - u0 : 256u * U;
+        prefetch_l2((threadIdx.x ? up : gate) + u0, (uint64_t)n * sizeof(float4));
+    }
     pdl_wait();
     pdl_trigger();
     const uint32_t base = blockIdx.x * (256u * U) + threadIdx.x;
@@ -181,6 +186,22 @@ __global__ void __launch_bounds__(128) combine_vec(const float4 *y, const int32_
 __global__ void __launch_bounds__(128) combine8_tokmajor(const float4 *y, const float *w, const float4 *residual,
                                                          float4 *out, uint32_t n_tokens, uint32_t cols4)
 {
+    {
+        // Lane k < 8 of each warp prefetches the warp's columns of expert row
+        // k into L2, lane 8 those of the residual (split where the warp's 32
+        // units straddle two tokens), while the previous kernel runs.
+        const uint32_t lane = threadIdx.x & 31, e0 = blockIdx.x * blockDim.x + (threadIdx.x & ~31u);
+        const uint32_t total = n_tokens * cols4;
+        if (lane < 9 && e0 < total) {
+            const uint32_t e1 = (e0 + 32 < total ? e0 + 32 : total);  // one past the warp's last unit
+            for (uint32_t a = e0; a < e1;) {
+                const uint32_t t = a / cols4, c = a - t * cols4;
+                const uint32_t n = (cols4 - c < e1 - a) ? cols4 - c : e1 - a;
+                prefetch_l2(lane < 8 ? y + (t * 8 + lane) * cols4 + c : residual + a, (uint64_t)n * sizeof(float4));
+                a += n;
+            }
+        }
+    }
     pdl_wait();
     pdl_trigger();
     const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;

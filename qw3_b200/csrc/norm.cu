@@ -84,12 +84,26 @@ __global__ void __launch_bounds__(32) add_rms_norm_bulk(const float *x, const fl
         mbar_init_fence();
     }
     __syncwarp();
+    int64_t cur = blockIdx.x;
+    // The weight is a static parameter: its bulk copy starts before the wait.
+    // The first x / r rows are only prefetched into L2 (they may be the
+    // previous kernel's output).
+    if (lane == 0) {
+        mbar_expect_tx(&bars[2], kRowBytes);
+        bulk_g2s(ws, w, kRowBytes, &bars[2]);
+        if (cur < rows) {
+            prefetch_l2(x + cur * n, kRowBytes);
+            if (r) prefetch_l2(r + cur * n, kRowBytes);
+        }
+    }
     pdl_wait();
     pdl_trigger();
 
     const int64_t stride = gridDim.x;
-    int64_t cur = blockIdx.x;
-    if (cur >= rows) return;
+    if (cur >= rows) {
+        mbar_wait(&bars[2], 0, kWaitLimit);  // the weight copy must land before the CTA exits
+        return;
+    }
     const uint32_t bytes = r ? 2 * kRowBytes : kRowBytes;
     auto issue = [&](int s, int64_t row) {
         if (lane == 0) {
@@ -98,12 +112,6 @@ __global__ void __launch_bounds__(32) add_rms_norm_bulk(const float *x, const fl
             if (r) bulk_g2s(buf[s][1], r + row * n, kRowBytes, &bars[s]);
         }
     };
-    // The weight comes in by one bulk copy issued with the first row, so the
-    // normed stores cost no second round trip.
-    if (lane == 0) {
-        mbar_expect_tx(&bars[2], kRowBytes);
-        bulk_g2s(ws, w, kRowBytes, &bars[2]);
-    }
     uint32_t parity = 0;
     int slot = 0;
     bool w_ready = false;

@@ -173,6 +173,18 @@ __global__ void __launch_bounds__(W * 32, tile_min_blocks<T, KV, W>()) qk_norm_r
             else if (nk > 0) wk[i - 128] = k_w[i - 128];
         }
     }
+    {
+        // The tile's q / k (/ v) rows are contiguous: one L2 prefetch each,
+        // issued while the previous kernel runs.
+        const int64_t tb = (int64_t)blockIdx.x * TT;
+        const int64_t nt = rows - tb < TT ? rows - tb : TT;
+        if ((tid & 31) == 0 && nt > 0) {
+            const int which = tid >> 5;
+            if (which == 0) prefetch_l2(q_src + tb * nq * 128, (uint64_t)nt * nq * 128 * sizeof(T));
+            else if (which == 1 && nk > 0) prefetch_l2(k_src + tb * nk * 128, (uint64_t)nt * nk * 128 * sizeof(T));
+            else if (KV && which == 2 && nk > 0) prefetch_l2(v_src + tb * nk * 128, (uint64_t)nt * nk * 128 * sizeof(T));
+        }
+    }
     pdl_wait();
     pdl_trigger();
 

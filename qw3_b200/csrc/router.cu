@@ -36,12 +36,13 @@ __global__ void __launch_bounds__(128) router_warp(const float *logits, float *p
                                                    int32_t *idx, float *scores, int64_t n_tokens,
                                                    int n_used, int norm_topk)
 {
-    pdl_wait();
-    pdl_trigger();
+    constexpr int E = 32 * V;
     const int lane = threadIdx.x & 31;
     const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (lane == 0 && t < n_tokens) prefetch_l2(logits + t * E, E * sizeof(float));
+    pdl_wait();
+    pdl_trigger();
     if (t >= n_tokens) return;
-    constexpr int E = 32 * V;
     const float *row = logits + t * E;
 
     float x[V];
