@@ -292,6 +292,31 @@ int ds3_cuda_router_logits_topk(const ds3_cuda_buffer_t *x, const ds3_cuda_buffe
                                 uint32_t n_tokens, uint32_t n_embd, uint32_t n_expert, uint32_t n_used,
                                 bool norm_topk_prob);
 
+/* ds3_metal.h:380-387. Router logits of one token, the weight in its stored
+ * type: gate_logits[e] = sum_i input[i] * W[e][i] (fp32, from 0, i
+ * ascending, multiply then add, as ds3_ref_vec_matmul over the dequantised
+ * weight), bit-exact. w_gate_inp: n_expert rows of n_embd elements of
+ * router_type (F32, F16, Q8_0, Q4_K, Q6_K), router_row_stride bytes apart
+ * (the GGUF nb[1]); input fp32 [n_embd]; gate_logits fp32 [n_expert]. A
+ * weight other than dense F32 is converted to fp32 in a library-owned
+ * device workspace first (n_expert * n_embd * 4 bytes, allocated on first
+ * use and kept): make the first such call outside a graph capture. */
+int ds3_cuda_moe_ffn_router(const ds3_cuda_buffer_t *input, const ds3_cuda_buffer_t *w_gate_inp,
+                            ds3_cuda_buffer_t *gate_logits, uint32_t n_embd, uint32_t n_expert,
+                            uint64_t router_row_stride, ds3_type_t router_type);
+
+/* new: moe_ffn_router for n_tokens rows of input [n_tokens, n_embd] fused
+ * with softmax + top-k + renorm (router_softmax_topk semantics): replaces
+ * ds3_metal_moe_ffn_router per token followed by moe_router_topk_batch_tokens
+ * (ds3_metal.h:437-445). gate_logits [n_tokens, n_expert] or NULL (required
+ * unless n_expert is 128 and n_embd a multiple of 64); idx / scores
+ * [n_tokens, n_used]. Same workspace rule as moe_ffn_router. */
+int ds3_cuda_moe_ffn_router_topk(const ds3_cuda_buffer_t *input, const ds3_cuda_buffer_t *w_gate_inp,
+                                 uint64_t router_row_stride, ds3_type_t router_type,
+                                 ds3_cuda_buffer_t *gate_logits, ds3_cuda_buffer_t *idx,
+                                 ds3_cuda_buffer_t *scores, uint32_t n_tokens, uint32_t n_embd,
+                                 uint32_t n_expert, uint32_t n_used, bool norm_topk_prob);
+
 /* SwiGLU with optional per-row routing weight:
  * out[r][c] = (silu(gate[r][c]) * up[r][c]) * row_weight[r]. row_weight may be
  * NULL (plain silu_mul, metal/moe.metal:95-108). */

@@ -53,6 +53,12 @@ struct State {
     bool capturing = false;
     bool profile = false;
     bool pdl = true;  // DS3_CUDA_PDL=0 disables programmatic dependent launch
+    // Library-owned device workspace: the fp32 copy of a router matrix stored
+    // in another type (moe_ffn_router*). Earlier, smaller allocations stay
+    // alive until shutdown: graphs captured before a growth still use them.
+    float *ws = nullptr;
+    size_t ws_bytes = 0;
+    std::vector<void *> ws_old;
     std::vector<cudaEvent_t> timers;
     std::vector<cudaEvent_t> event_pool;
     std::vector<ProfileRec> prof;
@@ -181,6 +187,28 @@ int finish(const char *op, cudaError_t launch, ProfScope &ps)
     return sync_and_check(op);
 }
 
+// At least `bytes` of library workspace, or nullptr (error set). It only
+// grows outside a graph capture (an allocation cannot be captured).
+float *workspace(const char *op, size_t bytes)
+{
+    if (G.ws_bytes >= bytes) return G.ws;
+    if (G.capturing) {
+        set_error("%s: the library workspace needs %zu bytes; make this call once outside a graph capture first",
+                  op, bytes);
+        return nullptr;
+    }
+    void *p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        set_error("%s: workspace of %zu bytes: %s", op, bytes, cudaGetErrorString(e));
+        return nullptr;
+    }
+    if (G.ws) G.ws_old.push_back(G.ws);
+    G.ws = (float *)p;
+    G.ws_bytes = bytes;
+    return G.ws;
+}
+
 int rope_freqs(uint32_t head_dim, float theta, float *freq)
 {
     // ds3_reference.c:369-377: freq_i = powf(theta, (float)i * (-2.0f / head_dim)).
@@ -305,6 +333,8 @@ void ds3_cuda_shutdown(void)
     for (auto e : G.timers)
         if (e) cudaEventDestroy(e);
     G.timers.clear();
+    if (G.ws) cudaFree(G.ws);
+    for (void *p : G.ws_old) cudaFree(p);
     cudaFreeHost(G.err_host);
     cudaStreamDestroy(G.stream);
     G = State();
@@ -922,6 +952,91 @@ int ds3_cuda_router_logits_topk(const ds3_cuda_buffer_t *x, const ds3_cuda_buffe
                                                n_tokens, (int)n_embd, (int)n_expert, (int)n_used,
                                                norm_topk_prob ? 1 : 0),
                   ps);
+}
+
+// Router projection with the weight in its stored type (F32, F16, Q8_0,
+// Q4_K or Q6_K rows, `row_stride` bytes apart, as the GGUF holds them). A
+// dense F32 matrix is used in place; any other is first converted to fp32 in
+// the library workspace by the bit-exact row dequant, so the logits equal
+// ds3_ref_vec_matmul over the reference's dequantised weights.
+static int moe_router_typed(const char *op, const ds3_cuda_buffer_t *input, const ds3_cuda_buffer_t *w,
+                            uint64_t row_stride, ds3_type_t type, ds3_cuda_buffer_t *logits, ds3_cuda_buffer_t *idx,
+                            ds3_cuda_buffer_t *scores, uint32_t n_tokens, uint32_t n_embd, uint32_t n_expert,
+                            uint32_t n_used, bool norm)
+{
+    if (!ready(op)) return -1;
+    uint64_t rb = 0;
+    if (n_embd == 0 || n_expert == 0 || !type_row_bytes(type, n_embd, &rb)) {
+        set_error("%s: unsupported router type %d or n_embd %u", op, (int)type, n_embd);
+        return -1;
+    }
+    if (row_stride < rb) {
+        set_error("%s: router_row_stride %llu < row bytes %llu", op, (unsigned long long)row_stride,
+                  (unsigned long long)rb);
+        return -1;
+    }
+    if (idx && (n_used == 0 || n_used > n_expert || n_used > 64)) {
+        set_error("%s: need 0 < n_used (%u) <= min(n_expert (%u), 64)", op, n_used, n_expert);
+        return -1;
+    }
+    const size_t ob = (size_t)n_tokens * n_used * 4;
+    if (!need(op, "input", input, (size_t)n_tokens * n_embd * 4) ||
+        !need(op, "w_gate_inp", w, (size_t)(row_stride * (n_expert - 1) + rb)) ||
+        (logits && (!need(op, "gate_logits", logits, (size_t)n_tokens * n_expert * 4) ||
+                    !writable(op, "gate_logits", logits))) ||
+        (idx && (!need(op, "idx", idx, ob) || !writable(op, "idx", idx) || !need(op, "scores", scores, ob) ||
+                 !writable(op, "scores", scores))))
+        return -1;
+    if (!logits && !idx) {
+        set_error("%s: no output buffer", op);
+        return -1;
+    }
+    if (n_tokens == 0) return 0;
+    const float *wf = (const float *)dptr(w);
+    ProfScope ps(op);
+    if ((int)type != 0 || row_stride != rb) {
+        float *buf = workspace(op, (size_t)n_expert * n_embd * 4);
+        if (!buf) {
+            ps.close();
+            return -1;
+        }
+        const cudaError_t e = ds3::launch_dequantize_rows(ctx(), (const uint8_t *)dptr(w), (int)type, row_stride,
+                                                          n_expert, (int)n_embd, buf);
+        if (e != cudaSuccess) return finish(op, e, ps);
+        wf = buf;
+    }
+    if (!logits && !ds3::router_gemv_fast(n_tokens, (int)n_embd, (int)n_expert, (int)n_used, dptr(input), wf)) {
+        set_error("%s: gate_logits is required for this shape (fast path: n_expert 128, n_embd %% 64 == 0)", op);
+        ps.close();
+        return -1;
+    }
+    return finish(op,
+                  ds3::launch_router_gemv_topk(ctx(), (const float *)dptr(input), wf, (float *)dptr(logits),
+                                               (int32_t *)dptr(idx), (float *)dptr(scores), n_tokens, (int)n_embd,
+                                               (int)n_expert, (int)(idx ? n_used : 0), norm ? 1 : 0),
+                  ps);
+}
+
+int ds3_cuda_moe_ffn_router(const ds3_cuda_buffer_t *input, const ds3_cuda_buffer_t *w_gate_inp,
+                            ds3_cuda_buffer_t *gate_logits, uint32_t n_embd, uint32_t n_expert,
+                            uint64_t router_row_stride, ds3_type_t router_type)
+{
+    return moe_router_typed("moe_ffn_router", input, w_gate_inp, router_row_stride, router_type, gate_logits,
+                            nullptr, nullptr, 1, n_embd, n_expert, 0, false);
+}
+
+int ds3_cuda_moe_ffn_router_topk(const ds3_cuda_buffer_t *input, const ds3_cuda_buffer_t *w_gate_inp,
+                                 uint64_t router_row_stride, ds3_type_t router_type, ds3_cuda_buffer_t *gate_logits,
+                                 ds3_cuda_buffer_t *idx, ds3_cuda_buffer_t *scores, uint32_t n_tokens,
+                                 uint32_t n_embd, uint32_t n_expert, uint32_t n_used, bool norm_topk_prob)
+{
+    const char *op = "moe_ffn_router_topk";
+    if (!idx || !scores) {
+        set_error("%s: idx and scores are required", op);
+        return -1;
+    }
+    return moe_router_typed(op, input, w_gate_inp, router_row_stride, router_type, gate_logits, idx, scores,
+                            n_tokens, n_embd, n_expert, n_used, norm_topk_prob);
 }
 
 int ds3_cuda_moe_expert_lists(const ds3_cuda_buffer_t *idx, const ds3_cuda_buffer_t *scores, ds3_cuda_buffer_t *counts,

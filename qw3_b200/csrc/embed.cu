@@ -363,6 +363,19 @@ __global__ void dequant_tensor_k(const uint8_t *src, int type, int64_t n, float 
         out[e] = dequant_one(type, src, (int)e);
 }
 
+// Rows of a stored matrix with any row stride (bytes) -> dense fp32 rows.
+__global__ void dequant_rows_k(const uint8_t *src, int type, uint64_t row_stride, int64_t n_rows, int n_cols,
+                               float *out)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int64_t n = n_rows * n_cols;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = e / n_cols;
+        out[e] = dequant_one(type, src + (uint64_t)r * row_stride, (int)(e - r * n_cols));
+    }
+}
+
 template <int TYPE, int NB>
 cudaError_t run_fast(const LaunchCtx &c, const EmbedArgs &a)
 {
@@ -439,6 +452,17 @@ cudaError_t launch_dequantize(const LaunchCtx &c, const uint8_t *src, int type, 
     int64_t blocks = (n + 255) / 256;
     if (blocks > 32LL * c.n_sm) blocks = 32LL * c.n_sm;
     launch_k(c, dequant_tensor_k, dim3((unsigned)blocks), dim3(256), src, type, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize_rows(const LaunchCtx &c, const uint8_t *src, int type, uint64_t row_stride,
+                                   int64_t n_rows, int n_cols, float *out)
+{
+    const int64_t n = n_rows * n_cols;
+    if (n <= 0) return cudaSuccess;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 32LL * c.n_sm) blocks = 32LL * c.n_sm;
+    launch_k(c, dequant_rows_k, dim3((unsigned)blocks), dim3(256), src, type, row_stride, n_rows, n_cols, out);
     return cudaGetLastError();
 }
 

@@ -61,6 +61,10 @@ cudaError_t launch_ks(const LaunchCtx &c, void (*k)(KArgs...), dim3 grid, dim3 b
 cudaError_t launch_add_rms_norm(const LaunchCtx &c, const float *x, const float *r, const float *w,
                                 float *sum_out, float *norm_out, int n, int64_t rows, float eps);
 
+// Rows of a stored matrix (row_stride bytes apart, any supported type) ->
+// dense fp32 [n_rows, n_cols], bit-exact with the reference dequant.
+cudaError_t launch_dequantize_rows(const LaunchCtx &c, const uint8_t *src, int type, uint64_t row_stride,
+                                   int64_t n_rows, int n_cols, float *out);
 // Whole tensor of `type` (F32, F16, Q8_0, Q4_K, Q6_K) to fp32; n < 2^31.
 cudaError_t launch_dequantize(const LaunchCtx &c, const uint8_t *src, int type, int64_t n, float *out);
 

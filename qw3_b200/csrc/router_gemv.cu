@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW>::kThreads, 1)
     }
     cluster_arrive_release();
     cluster_wait_acquire();
-    if (warp < L::kSel) {
+    if (idx && warp < L::kSel) {  // idx == nullptr: logits only
         const int tl = (int)rank * L::kSel + warp;  // this CTA selects for tokens kSel*rank ..
         if (tl < nt) {
             const float4 v = *reinterpret_cast<const float4 *>(lgx + warp * kRgE + 4 * lane);
@@ -292,6 +292,7 @@ cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const fl
                                     int n_used, int norm_topk)
 {
     if (n_tokens <= 0) return cudaSuccess;
+    if (!idx && !logits_out) return cudaErrorInvalidValue;
     if (router_gemv_fast(n_tokens, n_embd, n_expert, n_used, x, W))
         return launch_cluster<4, 4, 4, 4>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk);
     if (!logits_out) return cudaErrorInvalidValue;  // the general path needs the logits buffer
@@ -299,7 +300,7 @@ cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const fl
     launch_k(c, router_logits_k, dim3((unsigned)((n + 255) / 256)), dim3(256), x, W, logits_out, n_tokens, n_embd,
              n_expert);
     const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || !idx) return e;
     return launch_router_topk(c, logits_out, nullptr, idx, scores, n_tokens, n_expert, n_used, norm_topk);
 }
 

@@ -77,6 +77,8 @@ _SIGS = {
     "swiglu": (_I, [_P, _P, _P, _P, _U32, _U32]),
     "router_logits_topk": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _B]),
     "moe_expert_lists": (_I, [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32]),
+    "moe_ffn_router": (_I, [_P, _P, _P, _U32, _U32, _U64, _I]),
+    "moe_ffn_router_topk": (_I, [_P, _P, _U64, _I, _P, _P, _P, _U32, _U32, _U32, _U32, _B]),
     "moe_combine_residual": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32]),
     "stream": (_P, []),
     "graph_begin": (_I, []),
@@ -358,6 +360,18 @@ def router_logits_topk(x, w_router, logits_out, idx, scores, n_tokens, n_embd, n
                        norm_topk_prob=True) -> int:
     return lib().ds3_cuda_router_logits_topk(_h(x), _h(w_router), _h(logits_out), _h(idx), _h(scores), n_tokens,
                                              n_embd, n_expert, n_used, bool(norm_topk_prob))
+
+
+def moe_ffn_router(input_, w_gate_inp, gate_logits, n_embd, n_expert, router_row_stride, router_type) -> int:
+    return lib().ds3_cuda_moe_ffn_router(_h(input_), _h(w_gate_inp), _h(gate_logits), n_embd, n_expert,
+                                         router_row_stride, router_type)
+
+
+def moe_ffn_router_topk(input_, w_gate_inp, router_row_stride, router_type, gate_logits, idx, scores, n_tokens,
+                        n_embd, n_expert, n_used, norm_topk_prob=True) -> int:
+    return lib().ds3_cuda_moe_ffn_router_topk(_h(input_), _h(w_gate_inp), router_row_stride, router_type,
+                                              _h(gate_logits), _h(idx), _h(scores), n_tokens, n_embd, n_expert,
+                                              n_used, bool(norm_topk_prob))
 
 
 def moe_expert_lists(idx, scores, counts, ids, gscores, slot_of, n_tokens, n_expert, n_used, cap) -> int:
