@@ -317,6 +317,27 @@ int ds3_cuda_moe_ffn_router_topk(const ds3_cuda_buffer_t *input, const ds3_cuda_
                                  ds3_cuda_buffer_t *scores, uint32_t n_tokens, uint32_t n_embd,
                                  uint32_t n_expert, uint32_t n_used, bool norm_topk_prob);
 
+/* new, with no counterpart in the reference: moe_ffn_router_topk for callers
+ * that cannot let this library allocate device memory, for instance a host
+ * whose GPU memory is all reserved up front by its own allocator, or one
+ * that must not trigger an allocation (and its implicit device
+ * synchronisation) in the middle of a step. Same arguments, results and
+ * errors as moe_ffn_router_topk, but the fp32 copy of a router weight stored
+ * in another type goes into a fixed scratch array inside the loaded library
+ * (2 MiB per GPU that loads it, held until the process exits), so no call
+ * ever allocates device memory. Limit: n_expert * n_embd <= 524288 (128
+ * experts x 4096); larger shapes are refused with -1 and a message. The
+ * first call on a device looks up the array's device address (no
+ * allocation); make that first call before any stream capture. Every call
+ * shares the one array and leaves its last contents there (each call
+ * overwrites all it reads): calls that could run at the same time on the
+ * GPU, e.g. graphs replayed on different streams, race on it. */
+int ds3_cuda_moe_ffn_router_topk_noalloc(const ds3_cuda_buffer_t *input, const ds3_cuda_buffer_t *w_gate_inp,
+                                         uint64_t router_row_stride, ds3_type_t router_type,
+                                         ds3_cuda_buffer_t *gate_logits, ds3_cuda_buffer_t *idx,
+                                         ds3_cuda_buffer_t *scores, uint32_t n_tokens, uint32_t n_embd,
+                                         uint32_t n_expert, uint32_t n_used, bool norm_topk_prob);
+
 /* SwiGLU with optional per-row routing weight:
  * out[r][c] = (silu(gate[r][c]) * up[r][c]) * row_weight[r]. row_weight may be
  * NULL (plain silu_mul, metal/moe.metal:95-108). */

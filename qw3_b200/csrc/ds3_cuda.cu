@@ -1039,6 +1039,108 @@ int ds3_cuda_moe_ffn_router_topk(const ds3_cuda_buffer_t *input, const ds3_cuda_
                             n_tokens, n_embd, n_expert, n_used, norm_topk_prob);
 }
 
+// ---------------------------------------------- allocation-free router entry
+// A router call for callers that cannot let this library allocate device
+// memory: the fp32 copy of a stored router weight goes into a fixed scratch
+// array that is part of the loaded library (a file-scope __device__ array),
+// not into the workspace moe_ffn_router_topk allocates on first use. Every
+// GPU that loads the library holds the array until the process exits.
+static constexpr size_t kNoAllocRouterMaxElems = 524288;  // n_expert * n_embd; 2 MiB of fp32
+static __device__ __align__(256) float g_noalloc_router_scratch[kNoAllocRouterMaxElems];
+
+// Device address of the scratch array for the current device. The array's
+// name in host code is only a host-side stand-in, never a device address, so
+// the address is looked up once per device (with that device current) and
+// cached; the lookup allocates nothing.
+static float *noalloc_router_scratch(const char *op)
+{
+    constexpr int kMaxDevices = 64;
+    static float *addr[kMaxDevices] = {};
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        set_error("%s: no current device (%s)", op, e != cudaSuccess ? cudaGetErrorString(e) : "index out of range");
+        return nullptr;
+    }
+    if (!addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_router_scratch);
+        if (e != cudaSuccess || !p) {
+            set_error("%s: cudaGetSymbolAddress of the scratch array: %s", op, cudaGetErrorString(e));
+            return nullptr;
+        }
+        addr[dev] = static_cast<float *>(p);
+    }
+    return addr[dev];
+}
+
+int ds3_cuda_moe_ffn_router_topk_noalloc(const ds3_cuda_buffer_t *input, const ds3_cuda_buffer_t *w_gate_inp,
+                                         uint64_t router_row_stride, ds3_type_t router_type,
+                                         ds3_cuda_buffer_t *gate_logits, ds3_cuda_buffer_t *idx,
+                                         ds3_cuda_buffer_t *scores, uint32_t n_tokens, uint32_t n_embd,
+                                         uint32_t n_expert, uint32_t n_used, bool norm_topk_prob)
+{
+    const char *op = "moe_ffn_router_topk_noalloc";
+    if (!ready(op)) return -1;
+    uint64_t rb = 0;
+    if (n_embd == 0 || n_expert == 0 || !type_row_bytes(router_type, n_embd, &rb)) {
+        set_error("%s: unsupported router type %d or n_embd %u", op, (int)router_type, n_embd);
+        return -1;
+    }
+    if ((uint64_t)n_expert * n_embd > kNoAllocRouterMaxElems) {
+        set_error("%s: n_expert * n_embd = %llu exceeds the fixed scratch of %zu elements; use "
+                  "ds3_cuda_moe_ffn_router_topk",
+                  op, (unsigned long long)n_expert * n_embd, kNoAllocRouterMaxElems);
+        return -1;
+    }
+    if (router_row_stride < rb) {
+        set_error("%s: router_row_stride %llu < row bytes %llu", op, (unsigned long long)router_row_stride,
+                  (unsigned long long)rb);
+        return -1;
+    }
+    if (!idx || !scores || n_used == 0 || n_used > n_expert || n_used > 64) {
+        set_error("%s: need idx, scores and 0 < n_used (%u) <= min(n_expert (%u), 64)", op, n_used, n_expert);
+        return -1;
+    }
+    const size_t ob = (size_t)n_tokens * n_used * 4;
+    if (!need(op, "input", input, (size_t)n_tokens * n_embd * 4) ||
+        !need(op, "w_gate_inp", w_gate_inp, (size_t)(router_row_stride * (n_expert - 1) + rb)) ||
+        (gate_logits && (!need(op, "gate_logits", gate_logits, (size_t)n_tokens * n_expert * 4) ||
+                         !writable(op, "gate_logits", gate_logits))) ||
+        !need(op, "idx", idx, ob) || !writable(op, "idx", idx) || !need(op, "scores", scores, ob) ||
+        !writable(op, "scores", scores))
+        return -1;
+    float *scratch = noalloc_router_scratch(op);
+    if (!scratch) return -1;
+    if (n_tokens == 0) return 0;
+    const float *wf = (const float *)dptr(w_gate_inp);
+    if ((int)router_type != 0 || router_row_stride != rb) {
+        // Every element the projection reads is written here first, so the
+        // previous call's contents never need clearing.
+        const cudaError_t e = ds3::launch_dequantize_rows(ctx(), (const uint8_t *)dptr(w_gate_inp), (int)router_type,
+                                                          router_row_stride, n_expert, (int)n_embd, scratch);
+        if (e != cudaSuccess) {
+            set_error("%s: launch failed: %s", op, cudaGetErrorString(e));
+            return -1;
+        }
+        wf = scratch;
+    }
+    if (!gate_logits && !ds3::router_gemv_fast(n_tokens, (int)n_embd, (int)n_expert, (int)n_used, dptr(input), wf)) {
+        set_error("%s: gate_logits is required for this shape (fast path: n_expert 128, n_embd %% 64 == 0)", op);
+        return -1;
+    }
+    const cudaError_t e =
+        ds3::launch_router_gemv_topk(ctx(), (const float *)dptr(input), wf, (float *)dptr(gate_logits),
+                                     (int32_t *)dptr(idx), (float *)dptr(scores), n_tokens, (int)n_embd,
+                                     (int)n_expert, (int)n_used, norm_topk_prob ? 1 : 0);
+    if (e != cudaSuccess) {
+        set_error("%s: launch failed: %s", op, cudaGetErrorString(e));
+        return -1;
+    }
+    if (deferred()) return 0;
+    return sync_and_check(op);
+}
+
 int ds3_cuda_moe_expert_lists(const ds3_cuda_buffer_t *idx, const ds3_cuda_buffer_t *scores, ds3_cuda_buffer_t *counts,
                               ds3_cuda_buffer_t *ids, ds3_cuda_buffer_t *gscores, ds3_cuda_buffer_t *slot_of,
                               uint32_t n_tokens, uint32_t n_expert, uint32_t n_used, uint32_t cap)

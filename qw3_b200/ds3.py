@@ -79,6 +79,7 @@ _SIGS = {
     "moe_expert_lists": (_I, [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32]),
     "moe_ffn_router": (_I, [_P, _P, _P, _U32, _U32, _U64, _I]),
     "moe_ffn_router_topk": (_I, [_P, _P, _U64, _I, _P, _P, _P, _U32, _U32, _U32, _U32, _B]),
+    "moe_ffn_router_topk_noalloc": (_I, [_P, _P, _U64, _I, _P, _P, _P, _U32, _U32, _U32, _U32, _B]),
     "moe_combine_residual": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32]),
     "stream": (_P, []),
     "graph_begin": (_I, []),
@@ -372,6 +373,14 @@ def moe_ffn_router_topk(input_, w_gate_inp, router_row_stride, router_type, gate
     return lib().ds3_cuda_moe_ffn_router_topk(_h(input_), _h(w_gate_inp), router_row_stride, router_type,
                                               _h(gate_logits), _h(idx), _h(scores), n_tokens, n_embd, n_expert,
                                               n_used, bool(norm_topk_prob))
+
+
+def moe_ffn_router_topk_noalloc(input_, w_gate_inp, router_row_stride, router_type, gate_logits, idx, scores,
+                                n_tokens, n_embd, n_expert, n_used, norm_topk_prob=True) -> int:
+    """moe_ffn_router_topk without any device allocation (fixed in-library scratch)."""
+    return lib().ds3_cuda_moe_ffn_router_topk_noalloc(_h(input_), _h(w_gate_inp), router_row_stride, router_type,
+                                                      _h(gate_logits), _h(idx), _h(scores), n_tokens, n_embd,
+                                                      n_expert, n_used, bool(norm_topk_prob))
 
 
 def moe_expert_lists(idx, scores, counts, ids, gscores, slot_of, n_tokens, n_expert, n_used, cap) -> int:
