@@ -292,6 +292,23 @@ int ds3_cuda_router_logits_topk(const ds3_cuda_buffer_t *x, const ds3_cuda_buffe
                                 uint32_t n_tokens, uint32_t n_embd, uint32_t n_expert, uint32_t n_used,
                                 bool norm_topk_prob);
 
+/* new: the decode layer's FFN entry in one launch: residual add + ffn_norm
+ * RMSNorm + router projection + softmax + top-k + renorm. Replaces
+ * vec_add_inplace + buffer_copy_f32 + rms_norm + ds3_metal_moe_ffn_router +
+ * moe_router_topk_batch_tokens (src/ds3_engine.c:508-535). sum_out = x +
+ * residual (may alias residual or be NULL), norm_out = RMSNorm(sum) * weight
+ * (may be NULL), both bit-identical to ds3_cuda_add_rms_norm; logits and
+ * top-k as ds3_cuda_router_logits_topk over those normed rows (w_router fp32
+ * [n_expert][n_embd]; logits_out may be NULL). Needs n_expert 128, n_used <= 32,
+ * n_embd a multiple of 128 up to 2048 and 16-byte aligned rows; other shapes
+ * return -1 (use add_rms_norm, then router_logits_topk). */
+int ds3_cuda_add_rms_norm_router_topk(const ds3_cuda_buffer_t *x, const ds3_cuda_buffer_t *residual,
+                                      const ds3_cuda_buffer_t *norm_weight, const ds3_cuda_buffer_t *w_router,
+                                      ds3_cuda_buffer_t *sum_out, ds3_cuda_buffer_t *norm_out,
+                                      ds3_cuda_buffer_t *logits_out, ds3_cuda_buffer_t *idx,
+                                      ds3_cuda_buffer_t *scores, uint32_t n_tokens, uint32_t n_embd,
+                                      uint32_t n_expert, uint32_t n_used, float eps, bool norm_topk_prob);
+
 /* ds3_metal.h:380-387. Router logits of one token, the weight in its stored
  * type: gate_logits[e] = sum_i input[i] * W[e][i] (fp32, from 0, i
  * ascending, multiply then add, as ds3_ref_vec_matmul over the dequantised

@@ -954,6 +954,47 @@ int ds3_cuda_router_logits_topk(const ds3_cuda_buffer_t *x, const ds3_cuda_buffe
                   ps);
 }
 
+int ds3_cuda_add_rms_norm_router_topk(const ds3_cuda_buffer_t *x, const ds3_cuda_buffer_t *residual,
+                                      const ds3_cuda_buffer_t *norm_weight, const ds3_cuda_buffer_t *w_router,
+                                      ds3_cuda_buffer_t *sum_out, ds3_cuda_buffer_t *norm_out,
+                                      ds3_cuda_buffer_t *logits_out, ds3_cuda_buffer_t *idx, ds3_cuda_buffer_t *scores,
+                                      uint32_t n_tokens, uint32_t n_embd, uint32_t n_expert, uint32_t n_used,
+                                      float eps, bool norm_topk_prob)
+{
+    const char *op = "add_rms_norm_router_topk";
+    if (!ready(op)) return -1;
+    if (n_used == 0 || n_used > n_expert) {
+        set_error("%s: need 0 < n_used (%u) <= n_expert (%u)", op, n_used, n_expert);
+        return -1;
+    }
+    const size_t rb = (size_t)n_tokens * n_embd * 4, ob = (size_t)n_tokens * n_used * 4;
+    if (!need(op, "x", x, rb) || !need(op, "residual", residual, rb) ||
+        !need(op, "norm_weight", norm_weight, (size_t)n_embd * 4) ||
+        !need(op, "w_router", w_router, (size_t)n_expert * n_embd * 4) || !need(op, "idx", idx, ob) ||
+        !writable(op, "idx", idx) || !need(op, "scores", scores, ob) || !writable(op, "scores", scores) ||
+        (sum_out && (!need(op, "sum_out", sum_out, rb) || !writable(op, "sum_out", sum_out))) ||
+        (norm_out && (!need(op, "norm_out", norm_out, rb) || !writable(op, "norm_out", norm_out))) ||
+        (logits_out && (!need(op, "logits_out", logits_out, (size_t)n_tokens * n_expert * 4) ||
+                        !writable(op, "logits_out", logits_out))))
+        return -1;
+    if (n_tokens == 0) return 0;
+    if (!ds3::add_norm_router_fast(n_tokens, (int)n_embd, (int)n_expert, (int)n_used, dptr(x), dptr(residual),
+                                   dptr(w_router))) {
+        set_error("%s: needs n_expert 128, n_used <= 32, n_embd a multiple of 128 up to 2048 and 16-byte aligned "
+                  "rows (otherwise call add_rms_norm, then router_logits_topk)", op);
+        return -1;
+    }
+    ProfScope ps(op);
+    return finish(op,
+                  ds3::launch_add_norm_router_topk(ctx(), (const float *)dptr(x), (const float *)dptr(residual),
+                                                   (const float *)dptr(norm_weight), (const float *)dptr(w_router),
+                                                   (float *)dptr(sum_out), (float *)dptr(norm_out),
+                                                   (float *)dptr(logits_out), (int32_t *)dptr(idx),
+                                                   (float *)dptr(scores), n_tokens, (int)n_embd, (int)n_expert,
+                                                   (int)n_used, norm_topk_prob ? 1 : 0, eps),
+                  ps);
+}
+
 // Router projection with the weight in its stored type (F32, F16, Q8_0,
 // Q4_K or Q6_K rows, `row_stride` bytes apart, as the GGUF holds them). A
 // dense F32 matrix is used in place; any other is first converted to fp32 in

@@ -102,6 +102,14 @@ int kernel_binary_version();
 
 // Router projection (sequential fp32 dot products, reference order) + top-k.
 bool router_gemv_fast(int64_t n_tokens, int n_embd, int n_expert, int n_used, const void *x, const void *W);
+// Residual add + RMSNorm + router projection + top-k in one cluster kernel
+// (128 experts, n_embd % 128 == 0 and <= 2048, 16-byte aligned rows).
+bool add_norm_router_fast(int64_t n_tokens, int n_embd, int n_expert, int n_used, const void *x, const void *r,
+                          const void *W);
+cudaError_t launch_add_norm_router_topk(const LaunchCtx &c, const float *x, const float *r, const float *norm_w,
+                                        const float *W, float *sum_out, float *norm_out, float *logits_out,
+                                        int32_t *idx, float *scores, int64_t n_tokens, int n_embd, int n_expert,
+                                        int n_used, int norm_topk, float eps);
 cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const float *W, float *logits_out,
                                     int32_t *idx, float *scores, int64_t n_tokens, int n_embd, int n_expert,
                                     int n_used, int norm_topk);

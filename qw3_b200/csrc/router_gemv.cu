@@ -52,17 +52,34 @@ constexpr size_t kClMinSmem = 116 * 1024;    // > half an SM's shared memory: on
 // The launcher uses <4, 4, 4, 4>; at 512 tokens, 8x2 compute warps and 8 or
 // 12 copy warps measured the same or slower, and 1 or 2 copy warps or 2-CTA
 // clusters clearly slower.
-template <int CN, int NW, int TPW, int PW = kClPW>
+// FUSE: the token rows are not streamed through the ring; each CTA first
+// forms x + r and its RMSNorm for the cluster's tokens (add_rms_norm
+// semantics, same reduction order) into a normed-row area of up to
+// kFuseMaxEmbd floats per token, which the sums then read.
+constexpr int kFuseMaxEmbd = 2048;
+
+template <int CN, int NW, int TPW, int PW = kClPW, bool FUSE = false>
 struct ClLayout {
     static constexpr int kEpC = kRgE / CN;                            // experts per CTA
     static constexpr int kEpL = kEpC / 32;                            // experts per lane
     static constexpr int kThreads = 32 * (NW + PW);
     static constexpr int kTok = NW * TPW;                             // max tokens per cluster
     static constexpr int kSel = kTok / CN;                            // tokens each CTA selects for
-    static constexpr int kStageFloats = (kEpC + kTok) * kClLd;
-    static constexpr size_t kSmemUsed = (size_t)kClStages * kStageFloats * 4 + (size_t)kSel * kRgE * 4;
+    static constexpr int kStageFloats = (kEpC + (FUSE ? 0 : kTok)) * kClLd;
+    static constexpr size_t kNormFloats = FUSE ? (size_t)kTok * kFuseMaxEmbd : 0;
+    static constexpr size_t kSmemUsed =
+        (size_t)kClStages * kStageFloats * 4 + (size_t)kSel * kRgE * 4 + kNormFloats * 4;
     static constexpr size_t kSmem = kSmemUsed > kClMinSmem ? kSmemUsed : kClMinSmem;
     static_assert(kTok <= 32 && kTok % CN == 0 && kSel <= NW + PW && kEpC % 32 == 0, "layout");
+};
+
+// Arguments of the fused add + RMSNorm prologue (FUSE only).
+struct AddNorm {
+    const float *r;   // residual [n_tokens, n_embd]
+    const float *w;   // ffn_norm weight [n_embd]
+    float *sum_out;   // x + r, or nullptr
+    float *norm_out;  // normed rows, or nullptr
+    float eps;
 };
 
 __device__ __forceinline__ uint32_t cluster_rank()
@@ -94,14 +111,16 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t *bar)
 
 // tpc = tokens per cluster (<= NW * TPW), chosen by the host so that the
 // clusters fill the GPU in one wave.
-template <int CN, int NW, int TPW, int PW>
-__global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW>::kThreads, 1)
+template <int CN, int NW, int TPW, int PW, bool FUSE>
+__global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW, FUSE>::kThreads, 1)
     router_gemv_cluster_k(const float *x, const float *W, float *logits_out, int32_t *idx, float *scores,
-                          int64_t n_tokens, int n_embd, int n_used, int norm_topk, int tpc, unsigned *err)
+                          int64_t n_tokens, int n_embd, int n_used, int norm_topk, int tpc, unsigned *err,
+                          const AddNorm an)
 {
-    using L = ClLayout<CN, NW, TPW, PW>;
+    using L = ClLayout<CN, NW, TPW, PW, FUSE>;
     extern __shared__ __align__(16) float sm[];
     float *lgx = sm + kClStages * L::kStageFloats;  // [kSel][128] logits of the tokens this CTA selects for
+    float *xn = lgx + L::kSel * kRgE;               // FUSE: [kTok][n_embd] normed rows of the cluster's tokens
     __shared__ __align__(8) uint64_t full[kClStages], empty[kClStages];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -122,6 +141,35 @@ __global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW>::kThreads, 1)
     pdl_wait();
     pdl_trigger();
 
+    if constexpr (FUSE) {
+        // x + r and its RMSNorm for the cluster's tokens, one warp per token,
+        // with add_rms_norm's reduction (lane l sums the squares of float4
+        // l, l+32, ... in order, then a butterfly), so the normed rows equal
+        // that kernel's bit for bit. Every CTA of the cluster forms them in
+        // its own shared memory for its own sums; rank 0 writes sum_out /
+        // norm_out at the very end, after a cluster barrier, so outputs that
+        // alias x or r (the engine keeps the sum in the residual buffer) are
+        // never overwritten while another CTA still reads them.
+        const int vpl = n_embd / 128;
+        for (int tl = warp; tl < nt; tl += NW + PW) {
+            const int64_t t = t0 + tl;
+            const float4 *xr = reinterpret_cast<const float4 *>(x + t * n_embd);
+            const float4 *rr = reinterpret_cast<const float4 *>(an.r + t * n_embd);
+            float4 *xs = reinterpret_cast<float4 *>(xn + (size_t)tl * n_embd);
+            float ss = 0.0f;
+            for (int i = 0; i < vpl; i++) {
+                const float4 v = f4_add(__ldcg(xr + i * 32 + lane), __ldcg(rr + i * 32 + lane));
+                xs[i * 32 + lane] = v;
+                ss = f4_sumsq(v, ss);
+            }
+            ss = warp_sum(ss);
+            const float inv = rms_inv(ss, n_embd, an.eps);
+            const float4 *w4 = reinterpret_cast<const float4 *>(an.w);
+            for (int i = 0; i < vpl; i++) xs[i * 32 + lane] = f4_norm(xs[i * 32 + lane], inv, __ldg(w4 + i * 32 + lane));
+        }
+        __syncthreads();  // the normed rows are complete before any sum reads them
+    }
+
     bool ok = true;
     float acc[L::kEpL][TPW];
 #pragma unroll
@@ -141,7 +189,7 @@ __global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW>::kThreads, 1)
             }
             const int k0 = c * kClKC;
             float *st = sm + s * L::kStageFloats;
-            for (int q = pt; q < (L::kEpC + L::kTok) * kClSeg; q += 32 * PW) {
+            for (int q = pt; q < (L::kEpC + (FUSE ? 0 : L::kTok)) * kClSeg; q += 32 * PW) {
                 const int row = q / kClSeg, seg = q % kClSeg;
                 if (row < L::kEpC)
                     cp_async16(st + row * kClLd + 4 * seg, W + (int64_t)(e0 + row) * n_embd + k0 + 4 * seg);
@@ -160,7 +208,10 @@ __global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW>::kThreads, 1)
                 break;
             }
             const float *st = sm + s * L::kStageFloats;
-            const float *xr = st + (L::kEpC + warp * TPW) * kClLd;
+            // Token j of this warp: column k0 + 4i of its row (stage rows at
+            // stride kClLd, or the normed rows at stride n_embd).
+            const float *xr = FUSE ? xn + (size_t)(warp * TPW) * n_embd + c * kClKC : st + (L::kEpC + warp * TPW) * kClLd;
+            const int xld = FUSE ? n_embd : kClLd;
 #pragma unroll
             for (int i = 0; i < kClKC / 4; i++) {
                 float wv[L::kEpL][4];
@@ -175,7 +226,7 @@ __global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW>::kThreads, 1)
                 float pr[L::kEpL][TPW][4];
 #pragma unroll
                 for (int j = 0; j < TPW; j++) {
-                    const float4 v = *reinterpret_cast<const float4 *>(xr + j * kClLd + 4 * i);
+                    const float4 v = *reinterpret_cast<const float4 *>(xr + j * xld + 4 * i);
 #pragma unroll
                     for (int m = 0; m < L::kEpL; m++) {
                         const float2 p01 = mul2_rn(make_float2(v.x, v.y), make_float2(wv[m][0], wv[m][1]));
@@ -213,6 +264,25 @@ __global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW>::kThreads, 1)
     }
     cluster_arrive_release();
     cluster_wait_acquire();
+    if constexpr (FUSE) {
+        // Every CTA of the cluster has read x and r by now: rank 0 stores the
+        // sum (recomputed, the same single rounding) and the normed rows.
+        if (rank == 0 && (an.sum_out || an.norm_out)) {
+            const int vpl = n_embd / 128;
+            for (int tl = warp; tl < nt; tl += NW + PW) {
+                const int64_t t = t0 + tl;
+                const float4 *xr = reinterpret_cast<const float4 *>(x + t * n_embd);
+                const float4 *rr = reinterpret_cast<const float4 *>(an.r + t * n_embd);
+                const float4 *xs = reinterpret_cast<const float4 *>(xn + (size_t)tl * n_embd);
+                for (int i = 0; i < vpl; i++) {
+                    const int e = i * 32 + lane;
+                    const float4 sv = f4_add(__ldcg(xr + e), __ldcg(rr + e));
+                    if (an.sum_out) reinterpret_cast<float4 *>(an.sum_out + t * n_embd)[e] = sv;
+                    if (an.norm_out) reinterpret_cast<float4 *>(an.norm_out + t * n_embd)[e] = xs[e];
+                }
+            }
+        }
+    }
     if (idx && warp < L::kSel) {  // idx == nullptr: logits only
         const int tl = (int)rank * L::kSel + warp;  // this CTA selects for tokens kSel*rank ..
         if (tl < nt) {
@@ -224,12 +294,13 @@ __global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW>::kThreads, 1)
     }
 }
 
-template <int CN, int NW, int TPW, int PW = kClPW>
+template <int CN, int NW, int TPW, int PW = kClPW, bool FUSE = false>
 cudaError_t launch_cluster(const LaunchCtx &c, const float *x, const float *W, float *logits_out, int32_t *idx,
-                           float *scores, int64_t n_tokens, int n_embd, int n_used, int norm_topk)
+                           float *scores, int64_t n_tokens, int n_embd, int n_used, int norm_topk,
+                           const AddNorm &an = AddNorm{})
 {
-    using L = ClLayout<CN, NW, TPW, PW>;
-    auto kern = router_gemv_cluster_k<CN, NW, TPW, PW>;
+    using L = ClLayout<CN, NW, TPW, PW, FUSE>;
+    auto kern = router_gemv_cluster_k<CN, NW, TPW, PW, FUSE>;
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(L::kThreads);
     cfg.dynamicSmemBytes = L::kSmem;
@@ -259,7 +330,7 @@ cudaError_t launch_cluster(const LaunchCtx &c, const float *x, const float *W, f
     cfg.gridDim = dim3((unsigned)(((n_tokens + tpc - 1) / tpc) * CN));
     cfg.numAttrs = c.pdl ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk,
-                              (int)tpc, c.err);
+                              (int)tpc, c.err, an);
 }
 
 // Any shape: one thread per (token, expert) straight from global memory, same
@@ -302,6 +373,26 @@ cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const fl
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || !idx) return e;
     return launch_router_topk(c, logits_out, nullptr, idx, scores, n_tokens, n_expert, n_used, norm_topk);
+}
+
+bool add_norm_router_fast(int64_t n_tokens, int n_embd, int n_expert, int n_used, const void *x, const void *r,
+                          const void *W)
+{
+    const uintptr_t al = reinterpret_cast<uintptr_t>(r);
+    return router_gemv_fast(n_tokens, n_embd, n_expert, n_used, x, W) && n_embd % 128 == 0 &&
+           n_embd <= kFuseMaxEmbd && (al & 15u) == 0;
+}
+
+cudaError_t launch_add_norm_router_topk(const LaunchCtx &c, const float *x, const float *r, const float *norm_w,
+                                        const float *W, float *sum_out, float *norm_out, float *logits_out,
+                                        int32_t *idx, float *scores, int64_t n_tokens, int n_embd, int n_expert,
+                                        int n_used, int norm_topk, float eps)
+{
+    if (n_tokens <= 0) return cudaSuccess;
+    if (!add_norm_router_fast(n_tokens, n_embd, n_expert, n_used, x, r, W)) return cudaErrorInvalidValue;
+    const AddNorm an{r, norm_w, sum_out, norm_out, eps};
+    return launch_cluster<4, 4, 4, 4, true>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk,
+                                            an);
 }
 
 }  // namespace ds3

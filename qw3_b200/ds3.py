@@ -78,6 +78,7 @@ _SIGS = {
     "router_logits_topk": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _B]),
     "moe_expert_lists": (_I, [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32]),
     "moe_ffn_router": (_I, [_P, _P, _P, _U32, _U32, _U64, _I]),
+    "add_rms_norm_router_topk": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _F, _B]),
     "moe_ffn_router_topk": (_I, [_P, _P, _U64, _I, _P, _P, _P, _U32, _U32, _U32, _U32, _B]),
     "moe_ffn_router_topk_noalloc": (_I, [_P, _P, _U64, _I, _P, _P, _P, _U32, _U32, _U32, _U32, _B]),
     "moe_combine_residual": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32]),
@@ -361,6 +362,13 @@ def router_logits_topk(x, w_router, logits_out, idx, scores, n_tokens, n_embd, n
                        norm_topk_prob=True) -> int:
     return lib().ds3_cuda_router_logits_topk(_h(x), _h(w_router), _h(logits_out), _h(idx), _h(scores), n_tokens,
                                              n_embd, n_expert, n_used, bool(norm_topk_prob))
+
+
+def add_rms_norm_router_topk(x, residual, norm_weight, w_router, sum_out, norm_out, logits_out, idx, scores,
+                             n_tokens, n_embd, n_expert, n_used, eps, norm_topk_prob=True) -> int:
+    return lib().ds3_cuda_add_rms_norm_router_topk(_h(x), _h(residual), _h(norm_weight), _h(w_router), _h(sum_out),
+                                                   _h(norm_out), _h(logits_out), _h(idx), _h(scores), n_tokens,
+                                                   n_embd, n_expert, n_used, eps, bool(norm_topk_prob))
 
 
 def moe_ffn_router(input_, w_gate_inp, gate_logits, n_embd, n_expert, router_row_stride, router_type) -> int:

@@ -124,3 +124,42 @@ def test_moe_ffn_router_argument_errors(ds3, up):
     assert ds3.moe_ffn_router(x, wb, lb, 2048, 128, stride, 7) == -1       # unknown type
     assert ds3.moe_ffn_router(x, wb, lb, 2048, 256, stride, F16) == -1     # weight buffer too small
     assert ds3.moe_ffn_router_topk(x, wb, stride, F16, lb, None, None, 2, 2048, 128, 8, True) == -1
+
+
+@pytest.mark.parametrize("T,K,in_place", [(64, 2048, False), (64, 2048, True), (1, 2048, False), (512, 2048, False),
+                                          (37, 1024, True), (9, 128, False)])
+def test_add_rms_norm_router_topk(ds3, up, port, T, K, in_place):
+    """The decode FFN entry in one launch: the sum bit-exact with the oracle,
+    the normed rows bit-identical to add_rms_norm's (and within tolerance of
+    the oracle), the logits bit-exact with the reference's vec_matmul over
+    those normed rows, top-8 exact."""
+    E, n_used = 128, 8
+    x, r = I.normal(60 + T, (T, K)), I.normal(61 + T, (T, K))
+    w, W = I.gamma(K, 62), I.normal(63, (E, K), 0.0, 0.05)
+    xb, rb, wb, Wb = up(x), up(r), up(w), up(W)
+    so = rb if in_place else up(np.zeros((T, K), np.float32))
+    no, lb = up(np.zeros((T, K), np.float32)), up(np.zeros((T, E), np.float32))
+    ib, sb = up(np.zeros((T, n_used), np.int32)), up(np.zeros((T, n_used), np.float32))
+    rc = ds3.add_rms_norm_router_topk(xb, rb, wb, Wb, so, no, lb, ib, sb, T, K, E, n_used, 1e-6, True)
+    assert rc == 0, ds3.last_error()
+    s_want, n_want = port.add_rms_norm(x, r, w, 1e-6)
+    assert_bitexact(ds3.download(so, np.float32, (T, K)), s_want, "sum")
+    got_n = ds3.download(no, np.float32, (T, K))
+    assert_close(got_n, n_want, what="norm")
+    ref_n = up(np.zeros((T, K), np.float32))
+    assert ds3.add_rms_norm(up(x), up(r), wb, None, ref_n, K, T, 1e-6) == 0
+    assert_bitexact(got_n, ds3.download(ref_n, np.float32, (T, K)), "norm vs add_rms_norm")
+    lg = port.router_logits(got_n, W, 8)
+    _, want_i, want_s = port.router(lg, n_used, True)
+    assert_bitexact(ds3.download(lb, np.float32, (T, E)), lg, "logits")
+    assert_bitexact(ds3.download(ib, np.int32, (T, n_used)), want_i, "top-8")
+    assert_close(ds3.download(sb, np.float32, (T, n_used)), want_s, what="scores")
+
+
+def test_add_rms_norm_router_topk_rejects_other_shapes(ds3, up):
+    x = up(I.normal(1, (4, 2080)))
+    W = up(I.normal(2, (128, 2080)))
+    ib, sb = up(np.zeros((4, 8), np.int32)), up(np.zeros((4, 8), np.float32))
+    w = up(I.gamma(2080, 3))
+    assert ds3.add_rms_norm_router_topk(x, x, w, W, None, None, None, ib, sb, 4, 2080, 128, 8, 1e-6, True) == -1
+    assert "router_logits_topk" in ds3.last_error()
