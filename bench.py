@@ -1197,6 +1197,47 @@ def run_c2(ds3, O, thr, rec, up, empty, w, qw, kw, qw_h, kw_h, max_over_ranks, b
     ms = time_launches(ds3, [chain], 3, max_over_ranks, barrier)
     rec("c2_decode_B64_x48_layers_chain", B2, c2_bytes, ms,
         note="the engine's layer-by-layer order: 3 dependent launches per layer + final norm = 145 launches")
+
+    # The engine-faithful decode layer in 2 launches: QK-norm + RoPE, then
+    # residual add + ffn_norm + router projection (a seeded fp32 router
+    # weight per layer, N(0, 0.05)) + top-8 in one kernel; the router input
+    # is the normed hidden state, as in forward_layer_pre
+    # (src/ds3_engine.c:508-535), so the config's given logits are not used.
+    wr_h = [I.normal(6100 + l, (E, H), 0.0, 0.05) for l in range(L)]
+    wr = [up(a) for a in wr_h]
+
+    def chain2():
+        for l in range(L):
+            ds3.qk_norm_rope(view(q2, l, B2 * NQ * HD * 4), view(k2, l, B2 * NK * HD * 4), qw, kw,
+                             view(pos2, l, B2 * 4), B2, NQ, NK, HD, I.ROPE_THETA, eps)
+            ds3.add_rms_norm_router_topk(view(hid, l, B2 * H * 4), view(res, l, B2 * H * 4), w, wr[l],
+                                         view(sum_out, l, B2 * H * 4), view(nrm, l, B2 * H * 4), None,
+                                         view(ix, l, B2 * K * 4), view(sc, l, B2 * K * 4), B2, H, E, K, eps, True)
+        ds3.rms_norm(last, w, fin, H, B2, eps)
+
+    chain2()
+    ds3.synchronize()
+    # Parity of the fused entry on layers 0 and 47: sum exact, normed rows
+    # within tolerance, top-8 exact against the oracle's projection of the
+    # kernel's normed rows.
+    par = {}
+    got_s = ds3.download(sum_out, np.float32, (R, H))
+    got_n_all = ds3.download(nrm, np.float32, (R, H))
+    got_i = ds3.download(ix, np.int32, (R, K))
+    for l in (0, L - 1):
+        rows = slice(l * B2, (l + 1) * B2)
+        s_w, n_w = O.add_rms_norm(hid_h[rows], res_h[rows], w_h, eps, thr)
+        got_n = np.ascontiguousarray(got_n_all[rows])
+        _, iw2, _ = O.router(O.router_logits(got_n, wr_h[l], thr), K, True, thr)
+        par[f"l{l}_sum_bitexact"] = bitexact(np.ascontiguousarray(got_s[rows]), s_w)
+        par[f"l{l}_norm_tol_ratio"] = tol_ratio(got_n, n_w)
+        par[f"l{l}_top8_exact"] = bitexact(np.ascontiguousarray(got_i[rows]), iw2)
+    c2f_bytes = B2 * L * (32768 + 36868 + 64) + L * E * H * 4 + B2 * 16384
+    ms = time_launches(ds3, [chain2], 3, max_over_ranks, barrier)
+    rec("c2_decode_B64_x48_layers_chain_fused_router", B2, c2f_bytes, ms, par,
+        note="engine-faithful decode layer in 2 launches (qk_norm_rope; add_rms_norm_router_topk with the router "
+             "projection from a 1 MB fp32 weight per layer) + final norm = 97 launches; bytes include the router "
+             "weights")
     for v in views + [last]:
         v.free()
 

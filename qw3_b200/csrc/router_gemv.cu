@@ -57,6 +57,7 @@ constexpr size_t kClMinSmem = 116 * 1024;    // > half an SM's shared memory: on
 // semantics, same reduction order) into a normed-row area of up to
 // kFuseMaxEmbd floats per token, which the sums then read.
 constexpr int kFuseMaxEmbd = 2048;
+constexpr int64_t kSmallT = 128;  // token counts served with one token per compute warp
 
 template <int CN, int NW, int TPW, int PW = kClPW, bool FUSE = false>
 struct ClLayout {
@@ -150,24 +151,53 @@ __global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW, FUSE>::kThreads, 1)
         // norm_out at the very end, after a cluster barrier, so outputs that
         // alias x or r (the engine keeps the sum in the residual buffer) are
         // never overwritten while another CTA still reads them.
-        const int vpl = n_embd / 128;
-        for (int tl = warp; tl < nt; tl += NW + PW) {
-            const int64_t t = t0 + tl;
-            const float4 *xr = reinterpret_cast<const float4 *>(x + t * n_embd);
-            const float4 *rr = reinterpret_cast<const float4 *>(an.r + t * n_embd);
-            float4 *xs = reinterpret_cast<float4 *>(xn + (size_t)tl * n_embd);
-            float ss = 0.0f;
-            for (int i = 0; i < vpl; i++) {
-                const float4 v = f4_add(__ldcg(xr + i * 32 + lane), __ldcg(rr + i * 32 + lane));
-                xs[i * 32 + lane] = v;
-                ss = f4_sumsq(v, ss);
+        // Only the compute warps do this (they meet on named barrier 1), so
+        // the copy warps start streaming W at once. Loads are issued in
+        // batches of 8 float4 per lane before any is used (one round trip per
+        // batch instead of one per float4).
+        if (warp < NW) {
+            const int vpl = n_embd / 128;
+            for (int tl = warp; tl < nt; tl += NW) {
+                const int64_t t = t0 + tl;
+                const float4 *xr = reinterpret_cast<const float4 *>(x + t * n_embd);
+                const float4 *rr = reinterpret_cast<const float4 *>(an.r + t * n_embd);
+                float4 *xs = reinterpret_cast<float4 *>(xn + (size_t)tl * n_embd);
+                float ss = 0.0f;
+                for (int i0 = 0; i0 < vpl; i0 += 8) {
+                    float4 a[8], b[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++)
+                        if (i0 + u < vpl) {
+                            a[u] = __ldcg(xr + (i0 + u) * 32 + lane);
+                            b[u] = __ldcg(rr + (i0 + u) * 32 + lane);
+                        }
+#pragma unroll
+                    for (int u = 0; u < 8; u++)
+                        if (i0 + u < vpl) {
+                            const float4 v = f4_add(a[u], b[u]);
+                            xs[(i0 + u) * 32 + lane] = v;
+                            ss = f4_sumsq(v, ss);
+                        }
+                }
+                ss = warp_sum(ss);
+                const float inv = rms_inv(ss, n_embd, an.eps);
+                const float4 *w4 = reinterpret_cast<const float4 *>(an.w);
+                for (int i0 = 0; i0 < vpl; i0 += 8) {
+                    float4 wv[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++)
+                        if (i0 + u < vpl) wv[u] = __ldg(w4 + (i0 + u) * 32 + lane);
+#pragma unroll
+                    for (int u = 0; u < 8; u++)
+                        if (i0 + u < vpl) {
+                            const int e = (i0 + u) * 32 + lane;
+                            xs[e] = f4_norm(xs[e], inv, wv[u]);
+                        }
+                }
             }
-            ss = warp_sum(ss);
-            const float inv = rms_inv(ss, n_embd, an.eps);
-            const float4 *w4 = reinterpret_cast<const float4 *>(an.w);
-            for (int i = 0; i < vpl; i++) xs[i * 32 + lane] = f4_norm(xs[i * 32 + lane], inv, __ldg(w4 + i * 32 + lane));
+            // The normed rows are complete before any compute warp reads them.
+            asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");
         }
-        __syncthreads();  // the normed rows are complete before any sum reads them
     }
 
     bool ok = true;
@@ -274,11 +304,21 @@ __global__ void __launch_bounds__(ClLayout<CN, NW, TPW, PW, FUSE>::kThreads, 1)
                 const float4 *xr = reinterpret_cast<const float4 *>(x + t * n_embd);
                 const float4 *rr = reinterpret_cast<const float4 *>(an.r + t * n_embd);
                 const float4 *xs = reinterpret_cast<const float4 *>(xn + (size_t)tl * n_embd);
-                for (int i = 0; i < vpl; i++) {
-                    const int e = i * 32 + lane;
-                    const float4 sv = f4_add(__ldcg(xr + e), __ldcg(rr + e));
-                    if (an.sum_out) reinterpret_cast<float4 *>(an.sum_out + t * n_embd)[e] = sv;
-                    if (an.norm_out) reinterpret_cast<float4 *>(an.norm_out + t * n_embd)[e] = xs[e];
+                for (int i0 = 0; i0 < vpl; i0 += 8) {
+                    float4 a[8], b[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++)
+                        if (i0 + u < vpl) {
+                            a[u] = __ldcg(xr + (i0 + u) * 32 + lane);
+                            b[u] = __ldcg(rr + (i0 + u) * 32 + lane);
+                        }
+#pragma unroll
+                    for (int u = 0; u < 8; u++)
+                        if (i0 + u < vpl) {
+                            const int e = (i0 + u) * 32 + lane;
+                            if (an.sum_out) reinterpret_cast<float4 *>(an.sum_out + t * n_embd)[e] = f4_add(a[u], b[u]);
+                            if (an.norm_out) reinterpret_cast<float4 *>(an.norm_out + t * n_embd)[e] = xs[e];
+                        }
                 }
             }
         }
@@ -364,8 +404,14 @@ cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const fl
 {
     if (n_tokens <= 0) return cudaSuccess;
     if (!idx && !logits_out) return cudaErrorInvalidValue;
-    if (router_gemv_fast(n_tokens, n_embd, n_expert, n_used, x, W))
+    if (router_gemv_fast(n_tokens, n_embd, n_expert, n_used, x, W)) {
+        // Each sum is a chain of n_embd dependent adds, so a warp's time is set
+        // by how many tokens it holds; up to kSmallT tokens (decode batches)
+        // one token per compute warp keeps that chain 4x shorter.
+        if (n_tokens <= kSmallT)
+            return launch_cluster<4, 4, 1, 4>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk);
         return launch_cluster<4, 4, 4, 4>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk);
+    }
     if (!logits_out) return cudaErrorInvalidValue;  // the general path needs the logits buffer
     const int64_t n = n_tokens * n_expert;
     launch_k(c, router_logits_k, dim3((unsigned)((n + 255) / 256)), dim3(256), x, W, logits_out, n_tokens, n_embd,
@@ -391,6 +437,9 @@ cudaError_t launch_add_norm_router_topk(const LaunchCtx &c, const float *x, cons
     if (n_tokens <= 0) return cudaSuccess;
     if (!add_norm_router_fast(n_tokens, n_embd, n_expert, n_used, x, r, W)) return cudaErrorInvalidValue;
     const AddNorm an{r, norm_w, sum_out, norm_out, eps};
+    if (n_tokens <= kSmallT)
+        return launch_cluster<4, 4, 1, 4, true>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used,
+                                                norm_topk, an);
     return launch_cluster<4, 4, 4, 4, true>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk,
                                             an);
 }
