@@ -80,16 +80,17 @@ OPS = list(ALGO_BYTES)
 STEP_BYTES = sum(ALGO_BYTES.values())
 
 # DRAM traffic per launch measured with ncu (dram__bytes_read.sum +
-# dram__bytes_write.sum, --clock-control none) on this workload. Reads equal
+# dram__bytes_write.sum, --clock-control none), one capture per kernel on
+# this workload. Reads equal
 # the algorithmic input bytes; the outputs of one T=512 launch are still in
 # L2 when it ends, so no write traffic is attributed to the launch itself.
 NCU_TRAFFIC = {
-    "embed_rms_norm": 635648,
-    "qk_norm_rope": 9456896,
-    "add_rms_norm": 8411648,
-    "router_softmax_topk": 270080,
-    "swiglu": 25189632,
-    "moe_combine_residual": 37773056,
+    "embed_rms_norm": 638976,
+    "qk_norm_rope": 9458944,
+    "add_rms_norm": 8412416,
+    "router_softmax_topk": 271360,
+    "swiglu": 25192192,
+    "moe_combine_residual": 37777664,
 }
 
 N_SETS = 4  # input sets rotated between steps (each ~73 MB; together > 126 MB L2)
