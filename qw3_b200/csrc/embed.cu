@@ -205,10 +205,9 @@ __global__ void __launch_bounds__(kWarps * 32) embed_warp(const EmbedArgs a)
     // While the previous kernel runs: read this warp's first id past L1 and
     // prefetch that table row into L2 (a hint only: the id is read again
     // after the wait, and a stale or bad id just prefetches nothing useful).
-    if (cur < a.n_ids && lane == 0) {
-        const int32_t hint = __ldcg(a.ids + cur);
-        if (hint >= 0 && hint < a.n_vocab) prefetch_l2(a.table + (uint64_t)hint * a.row_stride, kRowBytes);
-    }
+    const int32_t hint = cur < a.n_ids ? __ldcg(a.ids + cur) : -1;
+    const bool hint_ok = hint >= 0 && hint < a.n_vocab;
+    if (lane == 0 && hint_ok) prefetch_l2(a.table + (uint64_t)hint * a.row_stride, kRowBytes);
     pdl_wait();
     pdl_trigger();
     if (cur >= a.n_ids) return;  // whole warp leaves together; no CTA barrier below
@@ -247,9 +246,24 @@ __global__ void __launch_bounds__(kWarps * 32) embed_warp(const EmbedArgs a)
 
     uint32_t parity = 0;  // bit s: phase parity to wait for on slot s
     int slot = 0;
+    // The first row's copy starts from the hinted id (now read after the
+    // wait, so the table row is current) while the id itself is read again;
+    // if the id changed meanwhile, that copy is let land and the right row is
+    // fetched. This saves the id's round trip on the common path.
+    if (hint_ok) issue(slot, hint);
     int32_t cur_id = a.ids[cur];
     bool cur_ok = cur_id >= 0 && cur_id < a.n_vocab;
-    if (cur_ok) issue(slot, cur_id);
+    if (cur_id != hint) {
+        if (hint_ok) {
+            if (!__all_sync(kFull, mbar_wait(&bars[wid][slot], 0, kWaitLimit))) {
+                if (lane == 0) flag_error(a.err, kErrWaitTimeout);
+                return;
+            }
+            parity ^= 1u;
+            __syncwarp();
+        }
+        if (cur_ok) issue(slot, cur_id);
+    }
 
     while (cur < a.n_ids) {
         const int64_t nxt = cur + stride;

@@ -479,3 +479,26 @@ def test_async_copies_in_a_batch(ds3, B):
     assert ds3.end_batch() == 0
     assert_bitexact(out, f32(ob, ds3, x.shape), "async read")
     assert ds3.buffer_write_async(xb, 8, x) == -1  # past the end
+
+
+def test_embed_ids_written_by_the_previous_kernel(ds3, B, port):
+    """The gather reads a hint of each id before its PDL wait. When the ids
+    are the output of the kernel just before it (here a vec_add that copies
+    new ids over old ones, bit patterns added to zero), a hint may be stale;
+    the rows must still be those of the final ids."""
+    vocab, T, n_cols = 4000, 512, 2048
+    tab = I.q4k_table(vocab, n_cols, 71)
+    t = B.up(tab)
+    zeros = B.up(np.zeros(T, np.float32))
+    dst = B.up(I.token_ids(T, 72, vocab))  # stale ids, valid but different
+    out = B.empty(T * n_cols * 4)
+    for rep in range(6):
+        new = I.token_ids(T, 80 + rep, vocab)
+        src = B.up(new)
+        assert ds3.begin_batch() == 0
+        assert ds3.vec_add(src, zeros, dst, T) == 0
+        assert ds3.embed_rows(t, dst, out, T, n_cols, vocab, ds3.TYPE_Q4_K, 1152) == 0
+        assert ds3.end_batch() == 0, ds3.last_error()
+        want = port.embed_rows(tab, 12, 1152, vocab, new, n_cols)[1]
+        assert_bitexact(f32(out, ds3, (T, n_cols)), want, f"rep {rep}")
+        ds3.buffer_write(dst, 0, I.token_ids(T, 90 + rep, vocab))
