@@ -330,21 +330,18 @@ cudaError_t launch_swiglu(const LaunchCtx &c, const float *gate, const float *up
     if (n <= 0) return cudaSuccess;
     if (cols % 4 == 0 && al16(gate) && al16(up) && al16(out)) {
         const int64_t units = n / 4;
-        // One wave: at most as many CTAs as can be resident at once (a second
-        // partial wave would double the latency at small sizes); each thread
-        // then streams units with kSwigluUnroll x 2 loads in flight.
         // Non-persistent blocks (measured, 4096 x 768: 7.9 us vs 9.7 us for the
-        // persistent grid-stride kernel; 32768 x 768: 46 us vs 56 us): one unit
-        // per thread up to ~2M units, two beyond.
+        // persistent grid-stride kernel; 32768 x 768: 46 us vs 56 us).
         if (units < ((int64_t)1 << 31)) {
             auto *g4 = reinterpret_cast<const float4 *>(gate);
             auto *u4 = reinterpret_cast<const float4 *>(up);
             auto *o4 = reinterpret_cast<float4 *>(out);
             const uint32_t uu = (uint32_t)units, c4 = (uint32_t)(cols / 4);
-            if (units <= ((int64_t)2 << 20))
-                launch_k(c, swiglu_blk<1>, dim3((uu + 255) / 256), dim3(256), g4, u4, row_w, o4, uu, c4);
-            else
-                launch_k(c, swiglu_blk<2>, dim3((uu + 511) / 512), dim3(256), g4, u4, row_w, o4, uu, c4);
+            // Two units per thread at every size: at the 4096 x 768 chunk shape the
+            // grid then nearly fits one resident wave, so the next kernel's CTAs
+            // become resident (and start their L2 prefetch) sooner; measured in
+            // the T=512 step 29.0 vs 29.7 us with one unit (3 or 4 units: 30.3).
+            launch_k(c, swiglu_blk<2>, dim3((uu + 511) / 512), dim3(256), g4, u4, row_w, o4, uu, c4);
             return cudaGetLastError();
         }
         // Beyond 2^31 units: the persistent grid-stride kernel with 64-bit indices.
