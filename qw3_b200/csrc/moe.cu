@@ -183,46 +183,66 @@ __global__ void __launch_bounds__(128) combine_vec(const float4 *y, const int32_
 // loads are volatile asm statements, so all are issued before the first is
 // consumed (the generic kernel lets the compiler interleave them with the
 // sum; measured at T=512: 7.3 vs 7.6-8.2 us).
+template <int U>
 __global__ void __launch_bounds__(128) combine8_tokmajor(const float4 *y, const float *w, const float4 *residual,
                                                          float4 *out, uint32_t n_tokens, uint32_t cols4)
 {
+    const uint32_t total = n_tokens * cols4;
+    const uint32_t base = blockIdx.x * (128u * U) + threadIdx.x;
     {
         // Lane k < 8 of each warp prefetches the warp's columns of expert row
         // k into L2, lane 8 those of the residual (split where the warp's 32
         // units straddle two tokens), while the previous kernel runs.
-        const uint32_t lane = threadIdx.x & 31, e0 = blockIdx.x * blockDim.x + (threadIdx.x & ~31u);
-        const uint32_t total = n_tokens * cols4;
-        if (lane < 9 && e0 < total) {
-            const uint32_t e1 = (e0 + 32 < total ? e0 + 32 : total);  // one past the warp's last unit
-            for (uint32_t a = e0; a < e1;) {
-                const uint32_t t = a / cols4, c = a - t * cols4;
-                const uint32_t n = (cols4 - c < e1 - a) ? cols4 - c : e1 - a;
-                prefetch_l2(lane < 8 ? y + (t * 8 + lane) * cols4 + c : residual + a, (uint64_t)n * sizeof(float4));
-                a += n;
+        const uint32_t lane = threadIdx.x & 31;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const uint32_t e0 = base - lane + 128u * u;
+            if (lane < 9 && e0 < total) {
+                const uint32_t e1 = (e0 + 32 < total ? e0 + 32 : total);  // one past the warp's last unit
+                for (uint32_t a = e0; a < e1;) {
+                    const uint32_t t = a / cols4, c = a - t * cols4;
+                    const uint32_t n = (cols4 - c < e1 - a) ? cols4 - c : e1 - a;
+                    prefetch_l2(lane < 8 ? y + (t * 8 + lane) * cols4 + c : residual + a, (uint64_t)n * sizeof(float4));
+                    a += n;
+                }
             }
         }
     }
     pdl_wait();
     pdl_trigger();
-    const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;
-    if (e >= n_tokens * cols4) return;
-    const uint32_t t = e / cols4, c = e - t * cols4;
-    float4 yv[8];
-    float wk[8];
+    float4 yv[U][8], res[U];
+    float wk[U][8];
 #pragma unroll
-    for (int k = 0; k < 8; k++) yv[k] = ld_stream_inflight(y + (t * 8 + k) * cols4 + c);
-    const float4 res = ld_stream_inflight(residual + e);
+    for (int u = 0; u < U; u++) {
+        const uint32_t e = base + 128u * u;
+        if (e >= total) continue;
+        const uint32_t t = e / cols4, c = e - t * cols4;
 #pragma unroll
-    for (int k = 0; k < 8; k++) wk[k] = __ldg(w + t * 8 + k);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-        acc.x = __fadd_rn(acc.x, __fmul_rn(wk[k], yv[k].x));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(wk[k], yv[k].y));
-        acc.z = __fadd_rn(acc.z, __fmul_rn(wk[k], yv[k].z));
-        acc.w = __fadd_rn(acc.w, __fmul_rn(wk[k], yv[k].w));
+        for (int k = 0; k < 8; k++) yv[u][k] = ld_stream_inflight(y + (t * 8 + k) * cols4 + c);
+        res[u] = ld_stream_inflight(residual + e);
     }
-    out[e] = f4_add(res, acc);
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        const uint32_t e = base + 128u * u;
+        if (e >= total) continue;
+        const uint32_t t = e / cols4;
+#pragma unroll
+        for (int k = 0; k < 8; k++) wk[u][k] = __ldg(w + t * 8 + k);
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        const uint32_t e = base + 128u * u;
+        if (e >= total) continue;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            acc.x = __fadd_rn(acc.x, __fmul_rn(wk[u][k], yv[u][k].x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(wk[u][k], yv[u][k].y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(wk[u][k], yv[u][k].z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(wk[u][k], yv[u][k].w));
+        }
+        out[e] = f4_add(res[u], acc);
+    }
 }
 
 __global__ void combine_scalar(const float *y, const int32_t *y_rows, const float *w,
@@ -371,7 +391,9 @@ cudaError_t launch_combine(const LaunchCtx &c, const float *y, const int32_t *y_
         auto *o4 = reinterpret_cast<float4 *>(out);
         if (n_used == 8 && !y_rows && total * 8 < ((int64_t)1 << 31)) {
             const uint32_t tt = (uint32_t)n_tokens, c4 = (uint32_t)cols4, tot = (uint32_t)total;
-            launch_k(c, combine8_tokmajor, dim3((tot + 127) / 128), dim3(128), y4, w, r4, o4, tt, c4);
+            // Two units per thread: half the threads, so the next kernel's CTAs
+            // find room to become resident early (T=512 step 29.3 -> 28.8 us).
+            launch_k(c, combine8_tokmajor<2>, dim3((tot + 255) / 256), dim3(128), y4, w, r4, o4, tt, c4);
             return cudaGetLastError();
         }
         if (n_used == 8)
