@@ -386,6 +386,8 @@ def main():
     ap.add_argument("--sets", type=int, default=N_SETS, help="input sets rotated to defeat L2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip the per-config kernel lines")
+    ap.add_argument("--shard-of", type=int, default=0, metavar="N",
+                    help="with --only-configs: run the C4/C5 row shard one GPU of N would hold")
     ap.add_argument("--only-configs", action="store_true",
                     help="run only the per-config kernels (a short command for ncu captures)")
     ap.add_argument("--profile", action="store_true", help="short run for ncu: no e2e, baseline or configs")
@@ -464,9 +466,9 @@ def main():
     table_host = I.q4k_table(V, H, 1)
     if args.only_configs:
         peak, _ = measured_peak()
-        cfg = run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_host)
+        cfg = run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_host, args.shard_of)
         if rank == 0:
-            emit({"configs": cfg})
+            emit({"configs": cfg, "shard_of": args.shard_of})
         return 0
     params_host = make_params()
     P = {"table": ds3.buffer_from_mmap(table_host)}
@@ -956,7 +958,7 @@ def n_copies(set_bytes: int, budget: int = 320_000_000, lo: int = 2) -> int:
     return max(lo, -(-budget // max(set_bytes, 1)))
 
 
-def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k):
+def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k, shard_of=0):
     """Kernel throughput on BASELINE configs 2-5 (per GPU; C4/C5 rows sharded
     across the ranks). Inputs rotate over copies larger than L2 on every rank.
     Before each config is timed, its first launch (on fresh inputs) is
@@ -1015,7 +1017,9 @@ def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k):
         if note:
             out[name]["note"] = note
 
-    a, b = shard_range(32768, world, rank)
+    # shard_of > 0: one GPU runs the row shard rank 0 would hold among
+    # shard_of GPUs (a single-GPU look at the per-GPU sizes of a larger run).
+    a, b = shard_range(32768, shard_of, 0) if shard_of else shard_range(32768, world, rank)
     n = b - a
     w = up(I.gamma(H, 3))
 
@@ -1105,24 +1109,28 @@ def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k):
     # on the rotated k and v), at the chunk size and at T=32768 (sharded).
     for tk in (512, n):
         msq = max(tk, 4096)
-        qv, kv_, vv = empty(tk * NQ * HD * 4), empty(tk * NK * HD * 4), empty(tk * NK * HD * 4)
-        ds3.buffer_write(qv, 0, I.normal(5100, (tk, NQ, HD)))
-        ds3.buffer_write(kv_, 0, I.normal(5101, (tk, NK, HD)))
-        ds3.buffer_write(vv, 0, I.normal(5102, (tk, NK, HD)))
-        kc, vc = empty(msq * NK * HD * 2), empty(msq * NK * HD * 2)
+        # Copies of q / k / v (and their own cache pair) that together exceed
+        # L2 on every rank, rotated between launches.
+        nkv = n_copies(tk * (NQ + 2 * NK) * HD * 4 + 2 * msq * NK * HD * 2)
+        qh5, kh5, vh5 = I.normal(5100, (tk, NQ, HD)), I.normal(5101, (tk, NK, HD)), I.normal(5102, (tk, NK, HD))
+        sets5 = []
+        for _ in range(nkv):
+            sets5.append((up(qh5), up(kh5), up(vh5), empty(msq * NK * HD * 2), empty(msq * NK * HD * 2)))
         pk = up(np.arange(tk, dtype=np.int32))
-        fused = [lambda: ds3.qk_norm_rope_kv(qv, kv_, vv, qw, kw, pk, kc, vc, tk, NQ, NK, HD, msq, I.ROPE_THETA, eps)]
+        fused = [lambda s5=s5: ds3.qk_norm_rope_kv(s5[0], s5[1], s5[2], qw, kw, pk, s5[3], s5[4], tk, NQ, NK, HD, msq,
+                                                   I.ROPE_THETA, eps) for s5 in sets5]
         fb = tk * (8 * (NQ + NK) * HD + 4 + 4 * NK * HD + 2 * 2 * NK * HD)
-        rec(f"qk_norm_rope_kv_write_T{tk}", tk, fb, time_launches(ds3, fused, 20, max_over_ranks, barrier),
-            note="fused: q/k in place + fp16 K/V cache rows (one input set: the chunk-size figure is L2-warm)")
+        rec(f"qk_norm_rope_kv_write_T{tk}", tk, fb, time_launches(ds3, fused, max(20, nkv), max_over_ranks, barrier),
+            note="fused: q/k in place + fp16 K/V cache rows", copies=nkv)
 
-        def two():
-            ds3.qk_norm_rope(qv, kv_, qw, kw, pk, tk, NQ, NK, HD, I.ROPE_THETA, eps)
-            ds3.kv_cache_write_batch(kv_, vv, kc, vc, 0, tk, msq, NQ, NK, HD)
+        def two(s5):
+            ds3.qk_norm_rope(s5[0], s5[1], qw, kw, pk, tk, NQ, NK, HD, I.ROPE_THETA, eps)
+            ds3.kv_cache_write_batch(s5[1], s5[2], s5[3], s5[4], 0, tk, msq, NQ, NK, HD)
 
-        rec(f"qk_norm_rope_then_kv_write_T{tk}", tk, fb, time_launches(ds3, [two], 20, max_over_ranks, barrier),
-            note="unfused reference sequence, same algorithmic bytes")
-        free(qv, kv_, vv, kc, vc, pk)
+        rec(f"qk_norm_rope_then_kv_write_T{tk}", tk, fb,
+            time_launches(ds3, [lambda s5=s5: two(s5) for s5 in sets5], max(20, nkv), max_over_ranks, barrier),
+            note="unfused reference sequence, same algorithmic bytes", copies=nkv)
+        free(pk, *[b for s5 in sets5 for b in s5])
 
     # Next-row kernel: device-side per-expert token lists for a 512-token
     # chunk (replaces the host loop + per-layer index readback of the engine).
