@@ -390,6 +390,253 @@ __global__ void router_logits_k(const float *x, const float *W, float *logits, i
     logits[q] = acc;
 }
 
+// ------------------------------------------------------------------------
+// Decode-size token counts (up to 8 tokens per cluster): the weight stays
+// resident. A cluster of 8 CTAs covers the 128 experts, CTA r holding rows
+// 16r .. 16r+15 of W whole in shared memory (one 1-D bulk copy per row, at a
+// padded stride), and the cluster's TOK token rows (or, fused, their
+// add + RMSNorm computed in place). Lane l of a compute warp sums expert
+// 16r + (l & 15) for token 2*warp + (l >> 4), i ascending, multiply then add
+// as the reference does: the only serial chain is the n_embd adds, with no
+// ring of stages to synchronise on. Logits go to the CTA whose rank is the
+// token (distributed shared memory), which then runs the selection.
+constexpr int kResE = 16;   // experts per CTA
+constexpr int kResCN = 8;   // CTAs per cluster
+constexpr int kResMaxEmbd = 2048;
+
+__host__ __device__ constexpr size_t res_smem(int tok, int n_embd)
+{
+    return ((size_t)kResE * (n_embd + 4) + (size_t)tok * n_embd + kRgE) * sizeof(float);
+}
+
+template <int TOK, bool FUSE>
+__global__ void __launch_bounds__(TOK * 16, 1)
+    router_gemv_resident_k(const float *x, const float *W, float *logits_out, int32_t *idx, float *scores,
+                           int64_t n_tokens, int n_embd, int n_used, int norm_topk, unsigned *err, const AddNorm an)
+{
+    extern __shared__ __align__(16) float sm[];
+    const int ldw = n_embd + 4;
+    float *ws = sm;                          // [16][ldw]
+    float *xs = ws + (size_t)kResE * ldw;    // [TOK][n_embd]
+    float *lg = xs + (size_t)TOK * n_embd;   // [128] logits of the token this CTA selects for
+    __shared__ __align__(8) uint64_t bar;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int64_t t0 = (int64_t)(blockIdx.x / kResCN) * TOK;
+    const int nt = n_tokens - t0 < TOK ? (int)(n_tokens - t0) : TOK;
+    const int e0 = (int)rank * kResE;
+    const uint32_t row_bytes = (uint32_t)n_embd * 4u;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_init_fence();
+        prefetch_l2(W + (size_t)e0 * n_embd, (uint64_t)kResE * row_bytes);
+        // The cluster's token rows: hints only (they may be the previous
+        // kernel's output; they are read after the wait).
+        prefetch_l2(x + t0 * n_embd, (uint64_t)nt * row_bytes);
+        if (FUSE) prefetch_l2(an.r + t0 * n_embd, (uint64_t)nt * row_bytes);
+    }
+    __syncthreads();
+    cluster_arrive_relaxed();
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        mbar_expect_tx(&bar, kResE * row_bytes + (FUSE ? 0u : (uint32_t)nt * row_bytes));
+        for (int j = 0; j < kResE; j++) bulk_g2s(ws + (size_t)j * ldw, W + (size_t)(e0 + j) * n_embd, row_bytes, &bar);
+        if constexpr (!FUSE)
+            for (int k = 0; k < nt; k++) bulk_g2s(xs + (size_t)k * n_embd, x + (t0 + k) * n_embd, row_bytes, &bar);
+    }
+    if constexpr (FUSE) {
+        // x + r and its RMSNorm (add_rms_norm's reduction order, so the normed
+        // rows equal that kernel's bit for bit), one warp per token; every CTA
+        // forms them for its own sums. The lane's share of the norm weight
+        // (static) is loaded once, the x / r rows of a token all at once.
+        const int vpl = n_embd / 128;  // <= 16
+        float4 wv[16];
+#pragma unroll
+        for (int u = 0; u < 16; u++)
+            if (u < vpl) wv[u] = __ldg(reinterpret_cast<const float4 *>(an.w) + u * 32 + lane);
+        for (int tl = warp; tl < nt; tl += TOK / 2) {
+            const int64_t t = t0 + tl;
+            const float4 *xr = reinterpret_cast<const float4 *>(x + t * n_embd);
+            const float4 *rr = reinterpret_cast<const float4 *>(an.r + t * n_embd);
+            float4 *xo = reinterpret_cast<float4 *>(xs + (size_t)tl * n_embd);
+            float4 a[16], b[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++)
+                if (u < vpl) {
+                    a[u] = __ldcg(xr + u * 32 + lane);
+                    b[u] = __ldcg(rr + u * 32 + lane);
+                }
+            float ss = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 16; u++)
+                if (u < vpl) {
+                    a[u] = f4_add(a[u], b[u]);
+                    ss = f4_sumsq(a[u], ss);
+                }
+            ss = warp_sum(ss);
+            const float inv = rms_inv(ss, n_embd, an.eps);
+#pragma unroll
+            for (int u = 0; u < 16; u++)
+                if (u < vpl) xo[u * 32 + lane] = f4_norm(a[u], inv, wv[u]);
+        }
+    }
+    bool ok = mbar_wait(&bar, 0, kWaitLimit);
+    __syncthreads();  // fused normed rows, and every thread past its wait
+    ok = __syncthreads_and(ok);
+    if (!ok && threadIdx.x == 0) flag_error(err, kErrWaitTimeout);
+
+    const int e = lane & 15, tk = 2 * warp + (lane >> 4);
+    float acc = 0.0f;
+    if (ok && tk < nt) {
+        // Software-pipelined over groups of 16 columns: the products of the
+        // next group (two IEEE products per mul.rn.f32x2) and the shared-memory
+        // reads of the group after it are issued before the 16 adds of the
+        // current group, so the chain of dependent adds is the only wait.
+        const float *wr = ws + (size_t)e * ldw;
+        const float *xr = xs + (size_t)tk * n_embd;
+        float pc[16], pn[16];
+        float4 wb[4], xb[4];
+        auto load = [&](int at) {
+#pragma unroll
+            for (int g = 0; g < 4; g++) {
+                wb[g] = *reinterpret_cast<const float4 *>(wr + at + 4 * g);
+                xb[g] = *reinterpret_cast<const float4 *>(xr + at + 4 * g);
+            }
+        };
+        auto products = [&](float *pr) {
+#pragma unroll
+            for (int g = 0; g < 4; g++) {
+                const float2 p01 = mul2_rn(make_float2(xb[g].x, xb[g].y), make_float2(wb[g].x, wb[g].y));
+                const float2 p23 = mul2_rn(make_float2(xb[g].z, xb[g].w), make_float2(wb[g].z, wb[g].w));
+                pr[4 * g] = p01.x;
+                pr[4 * g + 1] = p01.y;
+                pr[4 * g + 2] = p23.x;
+                pr[4 * g + 3] = p23.y;
+            }
+        };
+        load(0);
+        products(pc);
+        load(16 < n_embd ? 16 : 0);
+        for (int i = 0; i < n_embd; i += 16) {
+            products(pn);                                       // columns i+16 .. i+31
+            load(i + 32 < n_embd ? i + 32 : 0);                 // columns i+32 .. (unused past the end)
+#pragma unroll
+            for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, pc[u]);  // columns i .. i+15, in order
+#pragma unroll
+            for (int u = 0; u < 16; u++) pc[u] = pn[u];
+        }
+    }
+    cluster_wait_acquire();  // every CTA resident before the remote stores
+    if (tk < nt) {
+        if (logits_out) logits_out[(t0 + tk) * kRgE + e0 + e] = acc;
+        st_cluster_f32(lg + e0 + e, (uint32_t)tk, acc);
+    }
+    cluster_arrive_release();
+    cluster_wait_acquire();
+    if constexpr (FUSE) {
+        // Every CTA has read x and r: rank 0 stores the sum (recomputed, the
+        // same single rounding) and the normed rows.
+        if (rank == 0 && (an.sum_out || an.norm_out)) {
+            const int vpl = n_embd / 128;
+            for (int tl = warp; tl < nt; tl += TOK / 2) {
+                const int64_t t = t0 + tl;
+                const float4 *xr = reinterpret_cast<const float4 *>(x + t * n_embd);
+                const float4 *rr = reinterpret_cast<const float4 *>(an.r + t * n_embd);
+                const float4 *xo = reinterpret_cast<const float4 *>(xs + (size_t)tl * n_embd);
+                for (int i = 0; i < vpl; i++) {
+                    const int k = i * 32 + lane;
+                    const float4 sv = f4_add(__ldcg(xr + k), __ldcg(rr + k));
+                    if (an.sum_out) reinterpret_cast<float4 *>(an.sum_out + t * n_embd)[k] = sv;
+                    if (an.norm_out) reinterpret_cast<float4 *>(an.norm_out + t * n_embd)[k] = xo[k];
+                }
+            }
+        }
+    }
+    if (idx && warp == 0 && (int)rank < nt) {
+        const float4 v = *reinterpret_cast<const float4 *>(lg + 4 * lane);
+        const float xv[4] = {v.x, v.y, v.z, v.w};
+        const int64_t tw = t0 + rank;
+        router_select<4>(xv, lane, n_used, norm_topk, nullptr, idx + tw * n_used, scores + tw * n_used);
+    }
+}
+
+template <int TOK, bool FUSE>
+cudaError_t launch_resident(const LaunchCtx &c, const float *x, const float *W, float *logits_out, int32_t *idx,
+                            float *scores, int64_t n_tokens, int n_embd, int n_used, int norm_topk,
+                            const AddNorm &an)
+{
+    auto kern = router_gemv_resident_k<TOK, FUSE>;
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)res_smem(TOK, kResMaxEmbd));
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(((n_tokens + TOK - 1) / TOK) * kResCN));
+    cfg.blockDim = dim3(TOK * 16);
+    cfg.dynamicSmemBytes = res_smem(TOK, n_embd);
+    cfg.stream = c.stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kResCN;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = c.pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk, c.err,
+                              an);
+}
+
+// Clusters of 8 resident at once for the resident-weight kernel with TOK
+// tokens per cluster (queried once per TOK).
+template <int TOK>
+int resident_clusters()
+{
+    static int n = -1;
+    if (n < 0) {
+        auto kern = router_gemv_resident_k<TOK, false>;
+        n = 0;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)res_smem(TOK, kResMaxEmbd)) == cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(kResCN);
+            cfg.blockDim = dim3(TOK * 16);
+            cfg.dynamicSmemBytes = res_smem(TOK, kResMaxEmbd);
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = kResCN;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+        }
+        cudaGetLastError();
+    }
+    return n;
+}
+
+// Runs the resident-weight kernel when the shape allows it and one wave of
+// clusters covers the tokens; returns cudaErrorNotSupported otherwise.
+template <bool FUSE>
+cudaError_t try_resident(const LaunchCtx &c, const float *x, const float *W, float *logits_out, int32_t *idx,
+                         float *scores, int64_t n_tokens, int n_embd, int n_used, int norm_topk, const AddNorm &an)
+{
+    if (n_embd > kResMaxEmbd || n_embd % 128 != 0) return cudaErrorNotSupported;
+    if (n_tokens <= 2LL * resident_clusters<2>())
+        return launch_resident<2, FUSE>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk, an);
+    if (n_tokens <= 4LL * resident_clusters<4>())
+        return launch_resident<4, FUSE>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk, an);
+    if (n_tokens <= 8LL * resident_clusters<8>())
+        return launch_resident<8, FUSE>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk, an);
+    return cudaErrorNotSupported;
+}
+
 }  // namespace
 
 bool router_gemv_fast(int64_t n_tokens, int n_embd, int n_expert, int n_used, const void *x, const void *W)
@@ -408,6 +655,9 @@ cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const fl
         // Each sum is a chain of n_embd dependent adds, so a warp's time is set
         // by how many tokens it holds; up to kSmallT tokens (decode batches)
         // one token per compute warp keeps that chain 4x shorter.
+        const cudaError_t er =
+            try_resident<false>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk, AddNorm{});
+        if (er != cudaErrorNotSupported) return er;
         if (n_tokens <= kSmallT)
             return launch_cluster<4, 4, 1, 4>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk);
         return launch_cluster<4, 4, 4, 4>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk);
@@ -437,6 +687,8 @@ cudaError_t launch_add_norm_router_topk(const LaunchCtx &c, const float *x, cons
     if (n_tokens <= 0) return cudaSuccess;
     if (!add_norm_router_fast(n_tokens, n_embd, n_expert, n_used, x, r, W)) return cudaErrorInvalidValue;
     const AddNorm an{r, norm_w, sum_out, norm_out, eps};
+    const cudaError_t er = try_resident<true>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk, an);
+    if (er != cudaErrorNotSupported) return er;
     if (n_tokens <= kSmallT)
         return launch_cluster<4, 4, 1, 4, true>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used,
                                                 norm_topk, an);
