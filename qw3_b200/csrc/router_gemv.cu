@@ -404,13 +404,17 @@ constexpr int kResE = 16;   // experts per CTA
 constexpr int kResCN = 8;   // CTAs per cluster
 constexpr int kResMaxEmbd = 2048;
 
+// Threads per CTA: TOK / 2 summing warps, at least 4 warps (the fused
+// prologue gives each warp a token).
+__host__ __device__ constexpr int res_threads(int tok) { return tok * 16 > 128 ? tok * 16 : 128; }
+
 __host__ __device__ constexpr size_t res_smem(int tok, int n_embd)
 {
     return ((size_t)kResE * (n_embd + 4) + (size_t)tok * n_embd + kRgE) * sizeof(float);
 }
 
 template <int TOK, bool FUSE>
-__global__ void __launch_bounds__(TOK * 16, 1)
+__global__ void __launch_bounds__(res_threads(TOK), 1)
     router_gemv_resident_k(const float *x, const float *W, float *logits_out, int32_t *idx, float *scores,
                            int64_t n_tokens, int n_embd, int n_used, int norm_topk, unsigned *err, const AddNorm an)
 {
@@ -455,7 +459,7 @@ __global__ void __launch_bounds__(TOK * 16, 1)
 #pragma unroll
         for (int u = 0; u < 16; u++)
             if (u < vpl) wv[u] = __ldg(reinterpret_cast<const float4 *>(an.w) + u * 32 + lane);
-        for (int tl = warp; tl < nt; tl += TOK / 2) {
+        for (int tl = warp; tl < nt; tl += res_threads(TOK) / 32) {
             const int64_t t = t0 + tl;
             const float4 *xr = reinterpret_cast<const float4 *>(x + t * n_embd);
             const float4 *rr = reinterpret_cast<const float4 *>(an.r + t * n_embd);
@@ -535,21 +539,20 @@ __global__ void __launch_bounds__(TOK * 16, 1)
     cluster_arrive_release();
     cluster_wait_acquire();
     if constexpr (FUSE) {
-        // Every CTA has read x and r: rank 0 stores the sum (recomputed, the
-        // same single rounding) and the normed rows.
-        if (rank == 0 && (an.sum_out || an.norm_out)) {
-            const int vpl = n_embd / 128;
-            for (int tl = warp; tl < nt; tl += TOK / 2) {
+        // Every CTA has read x and r: each stores an eighth of the columns of
+        // every token's sum (recomputed, the same single rounding) and normed
+        // row, so outputs that alias x or r are only written now.
+        if (an.sum_out || an.norm_out) {
+            const int per = n_embd / 4 / kResCN;  // float4 columns per CTA
+            for (int q = threadIdx.x; q < nt * per; q += blockDim.x) {
+                const int tl = q / per, k = (int)rank * per + q % per;
                 const int64_t t = t0 + tl;
-                const float4 *xr = reinterpret_cast<const float4 *>(x + t * n_embd);
-                const float4 *rr = reinterpret_cast<const float4 *>(an.r + t * n_embd);
-                const float4 *xo = reinterpret_cast<const float4 *>(xs + (size_t)tl * n_embd);
-                for (int i = 0; i < vpl; i++) {
-                    const int k = i * 32 + lane;
-                    const float4 sv = f4_add(__ldcg(xr + k), __ldcg(rr + k));
-                    if (an.sum_out) reinterpret_cast<float4 *>(an.sum_out + t * n_embd)[k] = sv;
-                    if (an.norm_out) reinterpret_cast<float4 *>(an.norm_out + t * n_embd)[k] = xo[k];
-                }
+                const float4 xv = __ldcg(reinterpret_cast<const float4 *>(x + t * n_embd) + k);
+                const float4 rv = __ldcg(reinterpret_cast<const float4 *>(an.r + t * n_embd) + k);
+                if (an.sum_out) reinterpret_cast<float4 *>(an.sum_out + t * n_embd)[k] = f4_add(xv, rv);
+                if (an.norm_out)
+                    reinterpret_cast<float4 *>(an.norm_out + t * n_embd)[k] =
+                        reinterpret_cast<const float4 *>(xs + (size_t)tl * n_embd)[k];
             }
         }
     }
@@ -576,7 +579,7 @@ cudaError_t launch_resident(const LaunchCtx &c, const float *x, const float *W, 
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(((n_tokens + TOK - 1) / TOK) * kResCN));
-    cfg.blockDim = dim3(TOK * 16);
+    cfg.blockDim = dim3(res_threads(TOK));
     cfg.dynamicSmemBytes = res_smem(TOK, n_embd);
     cfg.stream = c.stream;
     cudaLaunchAttribute attr[2];
@@ -605,7 +608,7 @@ int resident_clusters()
                                  (int)res_smem(TOK, kResMaxEmbd)) == cudaSuccess) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(kResCN);
-            cfg.blockDim = dim3(TOK * 16);
+            cfg.blockDim = dim3(res_threads(TOK));
             cfg.dynamicSmemBytes = res_smem(TOK, kResMaxEmbd);
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
