@@ -20,7 +20,14 @@
  *    waits for the device and returns the status; inside a batch (or a graph
  *    capture) ops only enqueue, and end_batch waits and returns the status;
  *  - one device context per process (multi-GPU = one process per GPU; call
- *    ds3_cuda_set_device before ds3_cuda_init); state is not thread-safe.
+ *    ds3_cuda_set_device before ds3_cuda_init); state is not thread-safe;
+ *  - inside a batch or graph, consecutive ops overlap (programmatic dependent
+ *    launch): an op may read its weights (norm weights, the RoPE inputs'
+ *    q_w / k_w, the embedding table) before the op just before it has
+ *    finished. So a weight must not be written by the op immediately before
+ *    its use in the same batch or graph (make such a write, e.g. a
+ *    dequantize_f32 that produces a norm weight, outside the batch, or put
+ *    another op in between). Activations carry no such rule.
  *
  * Device-side errors (a token id outside the vocabulary, a bounded wait that
  * ran out) never trap: the kernel skips the bad row, writes zeros there and
