@@ -189,6 +189,49 @@ def enqueue_step(ds3, P, S, marks=None):
         raise RuntimeError("enqueue failed: " + ds3.last_error())
 
 
+# ------------------------------------------------------------------ NVML
+def nvml_handle(device_index: int):
+    """NVML handle of CUDA device `device_index` of this process, matched by
+    PCI address (NVML numbers devices physically, CUDA after
+    CUDA_VISIBLE_DEVICES), or None."""
+    try:
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        pr = torch.cuda.get_device_properties(device_index)
+        bus = "%08x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+        try:
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus.upper())
+    except Exception:
+        return None
+
+
+def bind_to_gpu_cpus(device_index: int):
+    """Run this rank on the host cores NVML lists as local to its GPU, so its
+    pinned host buffers are allocated (first touch) on the GPU's own NUMA node
+    and its copies do not cross the socket link. Returns the core count, or
+    None when NVML cannot tell (nothing is changed then)."""
+    h = nvml_handle(device_index)
+    if h is None:
+        return None
+    try:
+        import pynvml
+
+        n = os.cpu_count() or 1
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (n + 63) // 64)
+        cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1}
+        cpus &= set(os.sched_getaffinity(0))
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return len(cpus)
+    except Exception:
+        return None
+
+
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
     """Samples SM clock and throttle reasons through NVML while running."""
@@ -210,7 +253,9 @@ class ClockSampler:
 
             pynvml.nvmlInit()
             self.nv = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.h = nvml_handle(device_index)
+            if self.h is None:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
         except Exception:  # NVML unavailable: report nothing rather than guess
             self.nv = None
@@ -418,6 +463,9 @@ def main():
     import torch
 
     torch.cuda.set_device(local)
+    # Under torchrun every rank copies its own step inputs from pinned host
+    # memory (e2e); keep each rank on its GPU's local cores and memory.
+    host_cores = bind_to_gpu_cpus(local) if world > 1 else None
     if world > 1:
         import torch.distributed as dist
 
@@ -561,6 +609,7 @@ def main():
         "ms_per_step_per_rank": [round(m, 6) for m in per_rank],
         "slowest_rank": int(np.argmax(per_rank)),
         "pdl": bool(args.pdl),
+        "host_cores_per_rank": host_cores,
         "graphs": ("one graph per %d steps (a step on each input set in turn), replayed" % len(sets))
                   if cycle is not None else "one graph per step, replayed",
         "hbm_gbs_per_gpu": round(STEP_BYTES / (ms_step * 1e-3) / 1e9, 1),
