@@ -1200,11 +1200,88 @@ def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k, shar
     rec("router_logits_topk_T512", 512, 512 * (4 * H + 64) + E * H * 4, us_r,
         note="bit-exact sequential fp32 projection: %.0f GFLOP/s on CUDA cores" % (2 * 512 * E * H / (us_r * 1e-3) / 1e9))
 
+    run_c1_c3(ds3, O, thr, rec, up, empty, free, table_q4k, max_over_ranks, barrier)
     run_c2(ds3, O, thr, rec, up, empty, w, qw, kw, qw_h, kw_h, max_over_ranks, barrier)
 
     for x in list(bufs):
         x.free()
     return out
+
+
+def run_c1_c3(ds3, O, thr, rec, up, empty, free, table_q4k, max_over_ranks, barrier):
+    """BASELINE configs 1 and 3 on their own (the timed step contains both):
+      C1: layer-0 pre-attention chain on a 512-token chunk - Q4_K gather +
+          attn_norm, then QK-norm + RoPE at positions 0..511 (2 launches);
+      C3: routed-expert block - router softmax/top-8 on [512, 128], SwiGLU x
+          routing weight on [4096, 768], weighted combine + residual into
+          [512, 2048] (3 launches).
+    Inputs rotate over copies larger than L2; the first chain of each is
+    compared with the oracle."""
+    eps = I.NORM_EPS
+    par_h = make_params()
+    params = {k: up(v) for k, v in par_h.items()}
+    t4 = ds3.buffer_from_mmap(table_q4k)
+    # C1
+    c1_in = T * (4 + 4 * NQ * HD + 4 * NK * HD)
+    nc = n_copies(c1_in + 2 * T * H * 4)
+    hosts = [make_host_set(7000 + 13 * i) for i in range(2)]
+    sets = []
+    for i in range(nc):
+        hi = hosts[i % 2]
+        sets.append({"ids": up(hi["ids"]), "q": up(hi["q"]), "k": up(hi["k"]), "pos": up(hi["pos"]),
+                     "hid": empty(T * H * 4), "nrm": empty(T * H * 4)})
+
+    def c1(S):
+        ds3.embed_rms_norm(t4, S["ids"], params["attn_norm"], S["hid"], S["nrm"], T, H, V, ds3.TYPE_Q4_K, Q4K_ROW, eps)
+        ds3.qk_norm_rope(S["q"], S["k"], params["q_norm"], params["k_norm"], S["pos"], T, NQ, NK, HD, I.ROPE_THETA,
+                         eps)
+
+    c1(sets[0])
+    ds3.synchronize()
+    h = hosts[0]
+    _, wh, wn = O.embed_rms_norm(table_q4k, 12, Q4K_ROW, V, h["ids"], H, par_h["attn_norm"], eps, thr)
+    qo, ko = O.qk_norm_rope(h["q"], h["k"], par_h["q_norm"], par_h["k_norm"], h["pos"], I.ROPE_THETA, eps, thr)
+    par = {"hidden_bitexact": bitexact(ds3.download(sets[0]["hid"], np.float32, (T, H)), wh),
+           "norm_tol_ratio": tol_ratio(ds3.download(sets[0]["nrm"], np.float32, (T, H)), wn),
+           "qk_rope_tol_ratio": max(tol_ratio(ds3.download(sets[0]["q"], np.float32, qo.shape), qo),
+                                    tol_ratio(ds3.download(sets[0]["k"], np.float32, ko.shape), ko))}
+    c1_bytes = ALGO_BYTES["embed_rms_norm"] + ALGO_BYTES["qk_norm_rope"]
+    rec("c1_layer0_pre_T512", T, c1_bytes,
+        time_launches(ds3, [lambda S=S: c1(S) for S in sets], max(20, nc), max_over_ranks, barrier), par,
+        note="Q4_K gather + attn_norm, then QK-norm + RoPE: 2 dependent launches", copies=nc)
+    free(t4, *[b for S in sets for b in S.values()])
+
+    # C3
+    c3_bytes = ALGO_BYTES["router_softmax_topk"] + ALGO_BYTES["swiglu"] + ALGO_BYTES["moe_combine_residual"]
+    nc = n_copies(c3_bytes)
+    sets = []
+    for i in range(nc):
+        hi = hosts[i % 2]
+        sets.append({"logits": up(hi["logits"]), "gate": up(hi["gate"]), "up": up(hi["up"]), "y": up(hi["y"]),
+                     "res": up(hi["attn_out"]), "idx": empty(T * K * 4), "sc": empty(T * K * 4),
+                     "act": empty(T * K * FF * 4), "out": empty(T * H * 4)})
+
+    def c3(S):
+        ds3.router_softmax_topk(S["logits"], None, S["idx"], S["sc"], T, E, K, True)
+        ds3.swiglu(S["gate"], S["up"], S["sc"], S["act"], T * K, FF)
+        ds3.moe_combine_residual(S["y"], None, S["sc"], S["res"], S["out"], T, K, H)
+
+    c3(sets[0])
+    ds3.synchronize()
+    h = hosts[0]
+    _, iw, sw = O.router(h["logits"], K, True, thr)
+    got_sc = ds3.download(sets[0]["sc"], np.float32, (T, K))
+    par = {"top8_exact": bitexact(ds3.download(sets[0]["idx"], np.int32, (T, K)), iw),
+           "scores_tol_ratio": tol_ratio(got_sc, sw),
+           "swiglu_tol_ratio": tol_ratio(ds3.download(sets[0]["act"], np.float32, (T * K, FF)),
+                                         O.swiglu(h["gate"], h["up"], got_sc.reshape(-1), thr)),
+           "combine_bitexact": bitexact(ds3.download(sets[0]["out"], np.float32, (T, H)),
+                                        O.combine(h["y"], got_sc, h["attn_out"], None, thr))}
+    rec("c3_routed_expert_T512", T, c3_bytes,
+        time_launches(ds3, [lambda S=S: c3(S) for S in sets], max(20, nc), max_over_ranks, barrier), par,
+        note="router softmax/top-8, SwiGLU x routing weight, combine + residual: 3 dependent launches "
+             "(y [4096, 2048] stands in for the out-of-scope down projection)", copies=nc)
+    free(*[b for S in sets for b in S.values()], *params.values())
 
 
 def run_c2(ds3, O, thr, rec, up, empty, w, qw, kw, qw_h, kw_h, max_over_ranks, barrier):
