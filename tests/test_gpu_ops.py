@@ -481,14 +481,20 @@ def test_async_copies_in_a_batch(ds3, B):
     assert ds3.buffer_write_async(xb, 8, x) == -1  # past the end
 
 
-def test_embed_ids_written_by_the_previous_kernel(ds3, B, port):
-    """The gather reads a hint of each id before its PDL wait. When the ids
-    are the output of the kernel just before it (here a vec_add that copies
-    new ids over old ones, bit patterns added to zero), a hint may be stale;
-    the rows must still be those of the final ids."""
+@pytest.mark.parametrize("read_only_table", [False, True])
+def test_embed_ids_written_by_the_previous_kernel(ds3, B, port, read_only_table):
+    """The gather reads a hint of each id before its PDL wait. When the ids are
+    the output of
+    the kernel just before it (here a vec_add that copies new ids over old
+    ones, bit patterns added to zero), a hint may be stale; the rows must
+    still be those of the final ids."""
     vocab, T, n_cols = 4000, 512, 2048
     tab = I.q4k_table(vocab, n_cols, 71)
-    t = B.up(tab)
+    if read_only_table:
+        t = ds3.buffer_from_mmap(tab)
+        B.all.append(t)
+    else:
+        t = B.up(tab)
     zeros = B.up(np.zeros(T, np.float32))
     dst = B.up(I.token_ids(T, 72, vocab))  # stale ids, valid but different
     out = B.empty(T * n_cols * 4)
