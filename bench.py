@@ -440,6 +440,8 @@ def main():
                     help="time only QK-norm+RoPE with fp16 storage on T tokens (a small case for ncu)")
     ap.add_argument("--router-proj", type=int, default=0, metavar="T",
                     help="time only the router projection + top-8 on T tokens (a small case for ncu)")
+    ap.add_argument("--decode-ffn", type=int, default=0, metavar="T",
+                    help="time only the fused add + ffn_norm + router projection + top-8 on T tokens")
     ap.add_argument("--expert-lists", type=int, default=0, metavar="T",
                     help="time only the device per-expert token lists for T tokens (a small case for ncu)")
     ap.add_argument("--cycle-graph", type=int, default=1,
@@ -499,9 +501,11 @@ def main():
         torch.distributed.all_gather(parts, t)
         return [float(p.item()) for p in parts]
 
-    if args.rope_f16 or args.router_proj or args.expert_lists:
+    if args.rope_f16 or args.router_proj or args.expert_lists or args.decode_ffn:
         if args.rope_f16:
             line = run_rope_f16(ds3, args.rope_f16, max_over_ranks, barrier)
+        elif args.decode_ffn:
+            line = run_decode_ffn(ds3, args.decode_ffn, max_over_ranks, barrier)
         elif args.router_proj:
             line = run_router_proj(ds3, args.router_proj, max_over_ranks, barrier)
         else:
@@ -986,6 +990,20 @@ def run_router_proj(ds3, T, max_over_ranks, barrier):
         b.free()
     return {"workload": f"router_logits_topk_T{T}", "us": round(ms * 1e3, 3),
             "gflops": round(2 * T * E * H / (ms * 1e-3) / 1e9, 1)}
+
+
+def run_decode_ffn(ds3, T, max_over_ranks, barrier):
+    """The fused decode FFN entry alone on T tokens: residual add + ffn
+    RMSNorm + router projection + top-8 (ds3_cuda_add_rms_norm_router_topk)."""
+    x, r = ds3.upload(I.normal(7500, (T, H))), ds3.upload(I.normal(7501, (T, H)))
+    w, W = ds3.upload(I.gamma(H, 7502)), ds3.upload(I.normal(7503, (E, H), 0.0, 0.05))
+    so, no = ds3.empty(T * H * 4), ds3.empty(T * H * 4)
+    ix, sc = ds3.empty(T * K * 4), ds3.empty(T * K * 4)
+    fns = [lambda: ds3.add_rms_norm_router_topk(x, r, w, W, so, no, None, ix, sc, T, H, E, K, I.NORM_EPS, True)]
+    ms = time_launches(ds3, fns, 20, max_over_ranks, barrier)
+    for b in (x, r, w, W, so, no, ix, sc):
+        b.free()
+    return {"workload": f"add_rms_norm_router_topk_T{T}", "us": round(ms * 1e3, 3)}
 
 
 def run_expert_lists(ds3, T, max_over_ranks, barrier):
