@@ -89,8 +89,8 @@ NCU_TRAFFIC = {
     "qk_norm_rope": 9458944,
     "add_rms_norm": 8412416,
     "router_softmax_topk": 271360,
-    "swiglu": 25192192,
-    "moe_combine_residual": 37777664,
+    "swiglu": 25196544,
+    "moe_combine_residual": 37777408,
 }
 
 N_SETS = 4  # input sets rotated between steps (each ~73 MB; together > 126 MB L2)
