@@ -29,6 +29,9 @@ def up(ds3):
 
 
 @pytest.mark.parametrize("T,K,E,n_used,with_logits", [(512, 2048, 128, 8, True), (512, 2048, 128, 8, False),
+                                                      (2, 2048, 128, 8, False), (31, 2048, 128, 8, True),
+                                                      (97, 2048, 128, 8, False), (129, 2048, 128, 8, True),
+                                                      (150, 512, 128, 8, True), (300, 2048, 128, 32, True),
                                                       (1, 2048, 128, 8, True), (67, 1024, 128, 8, True),
                                                       (13, 100, 64, 4, True), (5, 2048, 32, 8, True),
                                                       (70, 2080, 128, 8, True), (1000, 2048, 128, 8, True)])
@@ -127,6 +130,7 @@ def test_moe_ffn_router_argument_errors(ds3, up):
 
 
 @pytest.mark.parametrize("T,K,in_place", [(64, 2048, False), (64, 2048, True), (1, 2048, False), (512, 2048, False),
+                                          (150, 2048, True), (300, 2048, False), (33, 256, True),
                                           (37, 1024, True), (9, 128, False)])
 def test_add_rms_norm_router_topk(ds3, up, port, T, K, in_place):
     """The decode FFN entry in one launch: the sum bit-exact with the oracle,
