@@ -16,7 +16,7 @@ out of scope; their outputs are seeded synthetic tensors of the right shapes.
 Scaling is weak: every GPU runs its own 512-token chunk, with no collective.
 
 value   : whole-job tokens/s over all N GPUs (the bench contract's aggregate;
-          tokens/s/GPU, the BASELINE metric's unit, is tokens_per_s_per_gpu =
+          tokens/s/GPU, the metric's own unit, is tokens_per_s_per_gpu =
           value / N), inputs resident in HBM (K graph replays, CUDA events on
           the module stream, barrier + synchronize both sides, max over ranks).
           Inputs rotate over several sets larger than L2 together.
@@ -686,7 +686,7 @@ def bitexact(got, want) -> bool:
 def check_outputs(O, table, params, g, out, threads):
     """Compare one step's outputs with the oracle on the same inputs: exact
     where the path is exact, else the worst error as a fraction of the
-    north-star tolerance (<= 1 passes)."""
+    stated tolerance: 1e-5 relative, 1e-6 absolute (<= 1 passes)."""
     eps = I.NORM_EPS
     res = {}
     _, hid, xn = O.embed_rms_norm(table, 12, Q4K_ROW, V, g["ids"], H, params["attn_norm"], eps, threads)
@@ -1026,7 +1026,7 @@ def n_copies(set_bytes: int, budget: int = 320_000_000, lo: int = 2) -> int:
 
 
 def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k, shard_of=0):
-    """Kernel throughput on BASELINE configs 2-5 (per GPU; C4/C5 rows sharded
+    """Kernel throughput on benchmark configs 2-5 (per GPU; C4/C5 rows sharded
     across the ranks). Inputs rotate over copies larger than L2 on every rank.
     Before each config is timed, its first launch (on fresh inputs) is
     compared with the oracle at the config's own size: `parity` in each entry
@@ -1227,7 +1227,7 @@ def run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_q4k, shar
 
 
 def run_c1_c3(ds3, O, thr, rec, up, empty, free, table_q4k, max_over_ranks, barrier):
-    """BASELINE configs 1 and 3 on their own (the timed step contains both):
+    """Benchmark configs 1 and 3 on their own (the timed step contains both):
       C1: layer-0 pre-attention chain on a 512-token chunk - Q4_K gather +
           attn_norm, then QK-norm + RoPE at positions 0..511 (2 launches);
       C3: routed-expert block - router softmax/top-8 on [512, 128], SwiGLU x

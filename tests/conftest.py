@@ -18,7 +18,7 @@ if str(ROOT) not in sys.path:
 
 GOLDEN = ROOT / "tests" / "golden"
 
-# Tolerances for fp32 outputs (north-star: 1e-5 relative, 1e-6 absolute).
+# Tolerances for fp32 outputs (1e-5 relative, 1e-6 absolute).
 RTOL, ATOL = 1e-5, 1e-6
 
 

@@ -1,7 +1,7 @@
 """GPU parity: every ds3_cuda entry point against the CPU oracle and the
 golden fixtures of the unmodified reference, through the C-ABI.
 
-Bars (north-star): bit-exact for embedding dequant, residual sums, the
+Bars (the tolerances the path is held to): bit-exact for embedding dequant, residual sums, the
 weighted combine and router top-k indices (exact ties excluded; the seeded
 inputs here have none); within 1e-5 relative / 1e-6 absolute for fp32 norm,
 RoPE, SwiGLU and softmax outputs; 2e-3 relative (1e-3 absolute floor) for the
