@@ -860,13 +860,19 @@ def run_e2e(ds3, P, S, host, steps, world, max_over_ranks, barrier):
 
     for _ in range(3):
         one()
+    # The host link is shared with whatever else the host does: its rate is
+    # measured right before and right after the e2e loop, and the better of
+    # the two is the roofline's denominator.
+    link0 = link_peak(ds3, h2d, d2h, max_over_ranks, barrier)
     barrier()
     t0 = time.perf_counter()
     for _ in range(n):
         one()
     el = max_over_ranks(time.perf_counter() - t0)
     barrier()
-    link = link_peak(ds3, h2d, d2h, max_over_ranks, barrier)
+    link1 = link_peak(ds3, h2d, d2h, max_over_ranks, barrier)
+    link = {k: max(link0[k], link1[k]) for k in link0}
+    link["before_after"] = [link0, link1]
     ms = 1e3 * el / n
     floor_ms = 1e3 * (h2d / (link["h2d_gbs"] * 1e9) + d2h / (link["d2h_gbs"] * 1e9))
     return {"value": round(world * T * n / el, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
@@ -875,7 +881,8 @@ def run_e2e(ds3, P, S, host, steps, world, max_over_ranks, barrier):
             "roofline": {"bound": "host link", "link": link, "floor_ms_per_step": round(floor_ms, 4),
                          "frac": round(floor_ms / ms, 4),
                          "note": "floor = the step's H2D bytes at the measured pinned H2D rate plus its D2H "
-                                 "bytes at the D2H rate, every rank copying at once"},
+                                 "bytes at the D2H rate, every rank copying at once; the better of the rates "
+                                 "measured just before and just after the e2e loop"},
             "api": "begin_batch / 9 x buffer_write_async (pinned) / 6 ops / 3 x buffer_read_async / end_batch "
                    "(wall clock)"}
 
@@ -892,7 +899,7 @@ def link_peak(ds3, h2d_bytes, d2h_bytes, max_over_ranks, barrier):
     out = {}
     for name, fn, nbytes in (("h2d", lambda: ds3.buffer_write_async(dev, 0, hb), h2d_bytes),
                              ("d2h", lambda: ds3.buffer_read_async(dev, 0, db), d2h_bytes)):
-        reps = max(5, int(2e9 // max(nbytes, 1)))
+        reps = max(5, int(8e9 // max(nbytes, 1)))
         for _ in range(2):
             fn()
         ds3.synchronize()
