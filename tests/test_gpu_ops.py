@@ -343,7 +343,7 @@ def test_swiglu_golden_and_silu_mul(ds3, B):
 
 
 @pytest.mark.parametrize("T,K,Cc,mapped", [(512, 8, 2048, False), (64, 8, 2048, True), (5, 4, 256, False),
-                                           (3, 8, 6, True)])
+                                           (3, 8, 6, True), (7, 8, 2056, False), (1, 8, 36, False)])
 def test_combine(ds3, B, port, T, K, Cc, mapped):
     y = I.normal(1, (T * K, Cc))
     w = I.rng(2).uniform(0, 1, (T, K)).astype(np.float32)
