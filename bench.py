@@ -628,7 +628,7 @@ def main():
     }
 
     if not args.profile:
-        line["e2e"] = run_e2e(ds3, P, sets[0], hosts[0], args.steps, world, max_over_ranks, barrier)
+        line["e2e"] = run_e2e(ds3, P, sets, hosts, args.steps, world, max_over_ranks, barrier)
         if not args.no_configs:
             line["configs"] = run_configs(ds3, world, rank, max_over_ranks, barrier, peak, table_host)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -827,78 +827,118 @@ def op_loops(ds3, P, max_over_ranks, barrier, peak, budget=320e6):
     return out
 
 
-def run_e2e(ds3, P, S, host, steps, world, max_over_ranks, barrier):
+def run_e2e(ds3, P, sets, hosts, steps, world, max_over_ranks, barrier):
     """Same step from pinned host memory: every input is copied host->device
-    and the step's outputs read back, inside the timed region."""
+    and the step's outputs read back, inside the timed region, through the
+    C-ABI. Two forms:
+      pipelined (the reported value): steps alternate between two device input
+        sets; step i+1's inputs arrive on copy lane 1 and step i-1's results
+        leave on copy lane 2 while step i computes on lane 0, ordered by
+        events (ds3_cuda_lane_*);
+      serial: one batch per step - copies in, the six ops, copies out."""
     import torch
 
     def pinned(a):
         t = torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
         return t.numpy()
 
-    src = {n: pinned(host[n]) for n in DevSet.IN}
-    outs = {"out": np.empty((T, H), np.float32), "idx": np.empty((T, K), np.int32),
-            "scores": np.empty((T, K), np.float32)}
-    outs = {n: pinned(a) for n, a in outs.items()}
-    h2d = sum(a.nbytes for a in src.values())
-    d2h = sum(a.nbytes for a in outs.values())
-    n = max(3, min(steps, 200))
+    src = [{n: pinned(h[n]) for n in DevSet.IN} for h in hosts[:2]]
 
-    def one():
-        # One batch per step: async copies in, the six ops, async copies out,
-        # then end_batch waits for all of it and checks the device error word.
-        ds3.begin_batch()
-        for name, a in src.items():
-            if ds3.buffer_write_async(S.b[name], 0, a) != 0:
-                raise RuntimeError(ds3.last_error())
-        enqueue_step(ds3, P, S)
-        for name, a in outs.items():
-            if ds3.buffer_read_async(S.b[name], 0, a) != 0:
-                raise RuntimeError(ds3.last_error())
-        if ds3.end_batch() != 0:
+    def out_bufs():
+        o = {"out": np.empty((T, H), np.float32), "idx": np.empty((T, K), np.int32),
+             "scores": np.empty((T, K), np.float32)}
+        return {n: pinned(a) for n, a in o.items()}
+
+    outs = [out_bufs(), out_bufs()]
+    h2d = sum(a.nbytes for a in src[0].values())
+    d2h = sum(a.nbytes for a in outs[0].values())
+    n = max(4, min(steps, 200))
+
+    def ok(rc):
+        if rc != 0:
             raise RuntimeError(ds3.last_error())
 
+    def serial_step():
+        ds3.begin_batch()
+        for name, a in src[0].items():
+            ok(ds3.buffer_write_async(sets[0].b[name], 0, a))
+        enqueue_step(ds3, P, sets[0])
+        for name, a in outs[0].items():
+            ok(ds3.buffer_read_async(sets[0].b[name], 0, a))
+        ok(ds3.end_batch())
+
+    # Event slots: inputs of set s uploaded / set s computed / set s read out.
+    UP, DONE, OUT = 100, 110, 120
+
+    def pipelined(k):
+        ok(ds3.begin_batch())
+        for i in range(k):
+            s = i % 2
+            S = sets[s]
+            if i >= 2:
+                ok(ds3.lane_wait(1, DONE + s))  # set s's inputs are free once step i-2 has run
+            for name, a in src[s].items():
+                ok(ds3.lane_write(1, S.b[name], 0, a))
+            ok(ds3.lane_record(1, UP + s))
+            ok(ds3.lane_wait(0, UP + s))
+            if i >= 2:
+                ok(ds3.lane_wait(0, OUT + s))  # step i-2's results have left set s
+            enqueue_step(ds3, P, S)
+            ok(ds3.lane_record(0, DONE + s))
+            ok(ds3.lane_wait(2, DONE + s))
+            for name, a in outs[s].items():
+                ok(ds3.lane_read(2, S.b[name], 0, a))
+            ok(ds3.lane_record(2, OUT + s))
+        ok(ds3.end_batch())
+
     for _ in range(3):
-        one()
+        serial_step()
+    pipelined(4)
     # The host link is shared with whatever else the host does: its rate is
-    # measured right before and right after the e2e loop, and the better of
+    # measured right before and right after the e2e loops, and the better of
     # the two is the roofline's denominator.
-    link0 = link_peak(ds3, h2d, d2h, max_over_ranks, barrier)
+    link0 = link_peak(ds3, sets[0], src[0], outs[0], max_over_ranks, barrier)
+    barrier()
+    t0 = time.perf_counter()
+    pipelined(n)
+    el = max_over_ranks(time.perf_counter() - t0)
     barrier()
     t0 = time.perf_counter()
     for _ in range(n):
-        one()
-    el = max_over_ranks(time.perf_counter() - t0)
+        serial_step()
+    el_serial = max_over_ranks(time.perf_counter() - t0)
     barrier()
-    link1 = link_peak(ds3, h2d, d2h, max_over_ranks, barrier)
+    link1 = link_peak(ds3, sets[0], src[0], outs[0], max_over_ranks, barrier)
     link = {k: max(link0[k], link1[k]) for k in link0}
     link["before_after"] = [link0, link1]
     ms = 1e3 * el / n
-    floor_ms = 1e3 * (h2d / (link["h2d_gbs"] * 1e9) + d2h / (link["d2h_gbs"] * 1e9))
+    # H2D and D2H use separate copy engines, so with the lanes the floor is
+    # the larger of the two directions (the ops hide under the copies).
+    floor_ms = 1e3 * max(h2d / (link["h2d_gbs"] * 1e9), d2h / (link["d2h_gbs"] * 1e9))
     return {"value": round(world * T * n / el, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(ms, 4),
             "copy_gbs": round((h2d + d2h) / (el / n) / 1e9, 2),
             "roofline": {"bound": "host link", "link": link, "floor_ms_per_step": round(floor_ms, 4),
                          "frac": round(floor_ms / ms, 4),
-                         "note": "floor = the step's H2D bytes at the measured pinned H2D rate plus its D2H "
-                                 "bytes at the D2H rate, every rank copying at once; the better of the rates "
-                                 "measured just before and just after the e2e loop"},
-            "api": "begin_batch / 9 x buffer_write_async (pinned) / 6 ops / 3 x buffer_read_async / end_batch "
-                   "(wall clock)"}
+                         "note": "floor = the step's H2D bytes at the pinned H2D rate of the same copies alone (the "
+                                 "D2H bytes overlap on the other copy engine), every rank copying at once; the "
+                                 "better of the rates measured just before and just after the e2e loops"},
+            "serial": {"value": round(world * T * n / el_serial, 1), "ms_per_step": round(1e3 * el_serial / n, 4),
+                       "api": "begin_batch / 9 x buffer_write_async / 6 ops / 3 x buffer_read_async / end_batch"},
+            "api": "one batch: per step, 9 x lane_write on copy lane 1, the 6 ops on lane 0, 3 x lane_read on lane 2, "
+                   "two device input sets alternating, ordered by lane_record / lane_wait (wall clock)"}
 
 
-def link_peak(ds3, h2d_bytes, d2h_bytes, max_over_ranks, barrier):
-    """Pinned host<->device copy rate through the same API (one large async
-    copy per direction on the module stream, wall clock, all ranks at once,
-    slowest rank), for the e2e roofline."""
-    import torch
-
-    hb = torch.empty(h2d_bytes, dtype=torch.uint8).pin_memory().numpy()
-    db = torch.empty(d2h_bytes, dtype=torch.uint8).pin_memory().numpy()
-    dev = ds3.empty(max(h2d_bytes, d2h_bytes))
+def link_peak(ds3, S, src, outs, max_over_ranks, barrier):
+    """Pinned host<->device copy rate of exactly the e2e step's transfers
+    (its 9 input copies, then its 3 output copies, repeated on the module
+    stream, wall clock, all ranks at once, slowest rank), for the e2e
+    roofline."""
+    h2d = sum(a.nbytes for a in src.values())
+    d2h = sum(a.nbytes for a in outs.values())
     out = {}
-    for name, fn, nbytes in (("h2d", lambda: ds3.buffer_write_async(dev, 0, hb), h2d_bytes),
-                             ("d2h", lambda: ds3.buffer_read_async(dev, 0, db), d2h_bytes)):
+    for name, fn, nbytes in (("h2d", lambda: [ds3.buffer_write_async(S.b[k], 0, a) for k, a in src.items()], h2d),
+                             ("d2h", lambda: [ds3.buffer_read_async(S.b[k], 0, a) for k, a in outs.items()], d2h)):
         reps = max(5, int(8e9 // max(nbytes, 1)))
         for _ in range(2):
             fn()
@@ -906,12 +946,11 @@ def link_peak(ds3, h2d_bytes, d2h_bytes, max_over_ranks, barrier):
         barrier()
         t0 = time.perf_counter()
         for _ in range(reps):
-            if fn() != 0:
+            if any(fn()):
                 raise RuntimeError(ds3.last_error())
         ds3.synchronize()
         el = max_over_ranks(time.perf_counter() - t0)
         out[f"{name}_gbs"] = round(nbytes * reps / el / 1e9, 2)
-    dev.free()
     barrier()
     return out
 

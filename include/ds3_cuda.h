@@ -382,6 +382,26 @@ int ds3_cuda_moe_combine_residual(const ds3_cuda_buffer_t *y, const ds3_cuda_buf
                                   uint32_t n_tokens, uint32_t n_used, uint32_t n_cols);
 
 /* ------------------------------------------------------------------ */
+/* Copy lanes (new): host transfers that overlap the ops              */
+/* ------------------------------------------------------------------ */
+
+/* Lane 0 is the module stream the ops run on; lanes 1 and 2 are two more
+ * streams for host<->device copies, so that the next step's inputs can
+ * arrive and the previous step's results leave while a step computes
+ * (each direction has its own copy engine). lane_write / lane_read enqueue
+ * a copy on a lane and do not wait (page-locked host memory, kept alive and
+ * unchanged until the lanes are synchronised). Ordering between lanes is the
+ * caller's: lane_record(lane, slot) records event slot `slot` (the timer
+ * slots) at the current end of `lane`, and lane_wait(lane, slot) makes
+ * everything enqueued on `lane` afterwards wait for it. ds3_cuda_synchronize
+ * and end_batch wait for all three lanes. Not available while capturing a
+ * graph. */
+int ds3_cuda_lane_write(int lane, ds3_cuda_buffer_t *buf, size_t offset, const void *src, size_t bytes);
+int ds3_cuda_lane_read(int lane, ds3_cuda_buffer_t *buf, size_t offset, void *dst, size_t bytes);
+int ds3_cuda_lane_record(int lane, int slot);
+int ds3_cuda_lane_wait(int lane, int slot);
+
+/* ------------------------------------------------------------------ */
 /* Streams, graphs, timers, errors (new)                              */
 /* ------------------------------------------------------------------ */
 

@@ -47,6 +47,7 @@ struct State {
     int device = 0;
     int n_sm = 148;
     cudaStream_t stream = nullptr;
+    cudaStream_t lanes[2] = {nullptr, nullptr};  // copy lanes 1 and 2 (lane 0 is `stream`)
     unsigned *err_host = nullptr;  // pinned + mapped; kErrSlots words
     unsigned *err_dev = nullptr;
     bool batch = false;
@@ -129,6 +130,8 @@ uint32_t take_device_errors()
 int sync_and_check(const char *op)
 {
     cudaError_t e = cudaStreamSynchronize(G.stream);
+    for (cudaStream_t l : G.lanes)
+        if (e == cudaSuccess && l) e = cudaStreamSynchronize(l);
     if (e != cudaSuccess) {
         set_error("%s: %s", op, cudaGetErrorString(e));
         return -1;
@@ -303,6 +306,11 @@ int ds3_cuda_init(void)
         set_error("init: stream: %s", cudaGetErrorString(e));
         return -1;
     }
+    for (cudaStream_t &l : G.lanes)
+        if ((e = cudaStreamCreateWithFlags(&l, cudaStreamNonBlocking)) != cudaSuccess) {
+            set_error("init: copy lane: %s", cudaGetErrorString(e));
+            return -1;
+        }
     if ((e = cudaHostAlloc((void **)&G.err_host, ds3::kErrSlots * sizeof(unsigned), cudaHostAllocMapped)) !=
         cudaSuccess) {
         set_error("init: error word: %s", cudaGetErrorString(e));
@@ -335,6 +343,11 @@ void ds3_cuda_shutdown(void)
     G.timers.clear();
     if (G.ws) cudaFree(G.ws);
     for (void *p : G.ws_old) cudaFree(p);
+    for (cudaStream_t l : G.lanes)
+        if (l) {
+            cudaStreamSynchronize(l);
+            cudaStreamDestroy(l);
+        }
     cudaFreeHost(G.err_host);
     cudaStreamDestroy(G.stream);
     G = State();
@@ -1245,6 +1258,98 @@ int ds3_cuda_moe_combine_residual(const ds3_cuda_buffer_t *y, const ds3_cuda_buf
                                       (const float *)dptr(w), (const float *)dptr(residual), (float *)dptr(out),
                                       n_tokens, (int)n_used, n_cols, (int64_t)(y->bytes / ((size_t)n_cols * 4))),
                   ps);
+}
+
+// ------------------------------------------------------------- copy lanes
+static cudaStream_t lane_stream(const char *op, int lane)
+{
+    if (!ready(op)) return nullptr;
+    if (G.capturing) {
+        set_error("%s: copy lanes are not available during graph capture", op);
+        return nullptr;
+    }
+    if (lane < 0 || lane > 2) {
+        set_error("%s: lane %d out of range 0..2", op, lane);
+        return nullptr;
+    }
+    return lane == 0 ? G.stream : G.lanes[lane - 1];
+}
+
+int ds3_cuda_lane_write(int lane, ds3_cuda_buffer_t *buf, size_t offset, const void *src, size_t bytes)
+{
+    const char *op = "lane_write";
+    cudaStream_t s = lane_stream(op, lane);
+    if (!s) return -1;
+    if (!buf || !src || offset + bytes > buf->bytes || buf->read_only) {
+        set_error("%s: bad arguments", op);
+        return -1;
+    }
+    const cudaError_t e = cudaMemcpyAsync((char *)dptr(buf) + offset, src, bytes, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) {
+        set_error("%s: %s", op, cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+int ds3_cuda_lane_read(int lane, ds3_cuda_buffer_t *buf, size_t offset, void *dst, size_t bytes)
+{
+    const char *op = "lane_read";
+    cudaStream_t s = lane_stream(op, lane);
+    if (!s) return -1;
+    if (!buf || !dst || offset + bytes > buf->bytes) {
+        set_error("%s: bad arguments", op);
+        return -1;
+    }
+    const cudaError_t e = cudaMemcpyAsync(dst, (char *)dptr(buf) + offset, bytes, cudaMemcpyDeviceToHost, s);
+    if (e != cudaSuccess) {
+        set_error("%s: %s", op, cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+static cudaEvent_t slot_event(const char *op, int slot)
+{
+    if (slot < 0 || slot >= DS3_CUDA_TIMER_SLOTS) {
+        set_error("%s: slot %d out of range", op, slot);
+        return nullptr;
+    }
+    if (!G.timers[slot] && cudaEventCreate(&G.timers[slot]) != cudaSuccess) {
+        set_error("%s: cudaEventCreate failed", op);
+        return nullptr;
+    }
+    return G.timers[slot];
+}
+
+int ds3_cuda_lane_record(int lane, int slot)
+{
+    const char *op = "lane_record";
+    cudaStream_t s = lane_stream(op, lane);
+    if (!s) return -1;
+    cudaEvent_t ev = slot_event(op, slot);
+    if (!ev) return -1;
+    const cudaError_t e = cudaEventRecord(ev, s);
+    if (e != cudaSuccess) {
+        set_error("%s: %s", op, cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+int ds3_cuda_lane_wait(int lane, int slot)
+{
+    const char *op = "lane_wait";
+    cudaStream_t s = lane_stream(op, lane);
+    if (!s) return -1;
+    cudaEvent_t ev = slot_event(op, slot);
+    if (!ev) return -1;
+    const cudaError_t e = cudaStreamWaitEvent(s, ev, 0);
+    if (e != cudaSuccess) {
+        set_error("%s: %s", op, cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
 }
 
 // --------------------------------------------------- stream / graph / timers

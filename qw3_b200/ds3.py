@@ -83,6 +83,10 @@ _SIGS = {
     "moe_ffn_router_topk_noalloc": (_I, [_P, _P, _U64, _I, _P, _P, _P, _U32, _U32, _U32, _U32, _B]),
     "moe_combine_residual": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32]),
     "stream": (_P, []),
+    "lane_write": (_I, [_I, _P, _SZ, _P, _SZ]),
+    "lane_read": (_I, [_I, _P, _SZ, _P, _SZ]),
+    "lane_record": (_I, [_I, _I]),
+    "lane_wait": (_I, [_I, _I]),
     "graph_begin": (_I, []),
     "graph_end": (_P, []),
     "graph_launch": (_I, [_P]),
@@ -226,6 +230,26 @@ def buffer_read_async(buf: Buffer, offset: int, host: np.ndarray) -> int:
     """Enqueue a device->host copy into `host`, valid after synchronize()."""
     assert host.flags["C_CONTIGUOUS"]
     return lib().ds3_cuda_buffer_read_async(_h(buf), offset, host.ctypes.data, host.nbytes)
+
+
+def lane_write(lane: int, buf: Buffer, offset: int, host: np.ndarray) -> int:
+    """Enqueue a host->device copy on copy lane `lane` (0 = the ops' stream)."""
+    assert host.flags["C_CONTIGUOUS"]
+    return lib().ds3_cuda_lane_write(lane, _h(buf), offset, host.ctypes.data, host.nbytes)
+
+
+def lane_read(lane: int, buf: Buffer, offset: int, host: np.ndarray) -> int:
+    """Enqueue a device->host copy on copy lane `lane`."""
+    assert host.flags["C_CONTIGUOUS"]
+    return lib().ds3_cuda_lane_read(lane, _h(buf), offset, host.ctypes.data, host.nbytes)
+
+
+def lane_record(lane: int, slot: int) -> int:
+    return lib().ds3_cuda_lane_record(lane, slot)
+
+
+def lane_wait(lane: int, slot: int) -> int:
+    return lib().ds3_cuda_lane_wait(lane, slot)
 
 
 def upload(host: np.ndarray) -> Buffer:

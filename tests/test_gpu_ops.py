@@ -508,3 +508,38 @@ def test_embed_ids_written_by_the_previous_kernel(ds3, B, port, read_only_table)
         want = port.embed_rows(tab, 12, 1152, vocab, new, n_cols)[1]
         assert_bitexact(f32(out, ds3, (T, n_cols)), want, f"rep {rep}")
         ds3.buffer_write(dst, 0, I.token_ids(T, 90 + rep, vocab))
+
+
+def test_copy_lanes_pipeline(ds3, B, port):
+    """Copy lanes: inputs uploaded on lane 1, the op on lane 0 after an event,
+    results read on lane 2 after another, two buffer sets alternating, as
+    bench.py's e2e pipeline does; every step's result equals the oracle's."""
+    import torch
+
+    n, steps = 1 << 16, 6
+    xs = [torch.from_numpy(I.normal(300 + i, (n // 2048, 2048))).pin_memory().numpy() for i in range(steps)]
+    rs = [torch.from_numpy(I.normal(400 + i, (n // 2048, 2048))).pin_memory().numpy() for i in range(steps)]
+    w = B.up(I.gamma(2048, 5))
+    outs = [torch.empty((n // 2048, 2048), dtype=torch.float32).pin_memory().numpy() for _ in range(steps)]
+    sets = [(B.empty(n * 4), B.empty(n * 4), B.empty(n * 4)) for _ in range(2)]
+    assert ds3.begin_batch() == 0
+    for i in range(steps):
+        s = i % 2
+        x, r, o = sets[s]
+        if i >= 2:
+            assert ds3.lane_wait(1, 210 + s) == 0
+        assert ds3.lane_write(1, x, 0, xs[i]) == 0 and ds3.lane_write(1, r, 0, rs[i]) == 0
+        assert ds3.lane_record(1, 200 + s) == 0
+        assert ds3.lane_wait(0, 200 + s) == 0
+        if i >= 2:
+            assert ds3.lane_wait(0, 220 + s) == 0
+        assert ds3.add_rms_norm(x, r, w, None, o, 2048, n // 2048, 1e-6) == 0
+        assert ds3.lane_record(0, 210 + s) == 0
+        assert ds3.lane_wait(2, 210 + s) == 0
+        assert ds3.lane_read(2, o, 0, outs[i]) == 0
+        assert ds3.lane_record(2, 220 + s) == 0
+    assert ds3.end_batch() == 0, ds3.last_error()
+    for i in range(steps):
+        _, want = port.add_rms_norm(xs[i], rs[i], I.gamma(2048, 5), 1e-6)
+        assert_close(outs[i], want, what=f"step {i}")
+    assert ds3.lane_write(3, sets[0][0], 0, xs[0]) == -1  # no such lane
