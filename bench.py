@@ -614,6 +614,8 @@ def main():
         "slowest_rank": int(np.argmax(per_rank)),
         "pdl": bool(args.pdl),
         "host_cores_per_rank": host_cores,
+        "process_group": ({"backend": torch.distributed.get_backend(), "world_size": torch.distributed.get_world_size()}
+                          if world > 1 else None),
         "graphs": ("one graph per %d steps (a step on each input set in turn), replayed" % len(sets))
                   if cycle is not None else "one graph per step, replayed",
         "hbm_gbs_per_gpu": round(STEP_BYTES / (ms_step * 1e-3) / 1e9, 1),
