@@ -23,7 +23,7 @@
  *    ds3_cuda_set_device before ds3_cuda_init); state is not thread-safe;
  *  - inside a batch or graph, consecutive ops overlap (programmatic dependent
  *    launch): an op may read its weights (norm weights, the RoPE inputs'
- *    q_w / k_w, the embedding table) before the op just before it has
+ *    q_w / k_w, the embedding table, an fp32 router weight) before the op just before it has
  *    finished. So a weight must not be written by the op immediately before
  *    its use in the same batch or graph (make such a write, e.g. a
  *    dequantize_f32 that produces a norm weight, outside the batch, or put

@@ -963,7 +963,7 @@ int ds3_cuda_router_logits_topk(const ds3_cuda_buffer_t *x, const ds3_cuda_buffe
                   ds3::launch_router_gemv_topk(ctx(), (const float *)dptr(x), (const float *)dptr(w_router),
                                                (float *)dptr(logits_out), (int32_t *)dptr(idx), (float *)dptr(scores),
                                                n_tokens, (int)n_embd, (int)n_expert, (int)n_used,
-                                               norm_topk_prob ? 1 : 0),
+                                               norm_topk_prob ? 1 : 0, true),
                   ps);
 }
 

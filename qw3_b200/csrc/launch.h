@@ -110,9 +110,11 @@ cudaError_t launch_add_norm_router_topk(const LaunchCtx &c, const float *x, cons
                                         const float *W, float *sum_out, float *norm_out, float *logits_out,
                                         int32_t *idx, float *scores, int64_t n_tokens, int n_embd, int n_expert,
                                         int n_used, int norm_topk, float eps);
+// w_static: W is the caller's weight, which no op immediately before writes,
+// so its copy may start before the programmatic-launch wait.
 cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const float *W, float *logits_out,
                                     int32_t *idx, float *scores, int64_t n_tokens, int n_embd, int n_expert,
-                                    int n_used, int norm_topk);
+                                    int n_used, int norm_topk, bool w_static = false);
 
 cudaError_t launch_router_topk(const LaunchCtx &c, const float *logits, float *probs_out,
                                int32_t *idx, float *scores, int64_t n_tokens, int n_expert,

@@ -81,6 +81,7 @@ struct AddNorm {
     float *sum_out;   // x + r, or nullptr
     float *norm_out;  // normed rows, or nullptr
     float eps;
+    int w_early;      // W is a weight no preceding op writes: its copy may start before the PDL wait
 };
 
 __device__ __forceinline__ uint32_t cluster_rank()
@@ -430,10 +431,20 @@ __global__ void __launch_bounds__(res_threads(TOK), 1)
     const int nt = n_tokens - t0 < TOK ? (int)(n_tokens - t0) : TOK;
     const int e0 = (int)rank * kResE;
     const uint32_t row_bytes = (uint32_t)n_embd * 4u;
+    const uint32_t tx = kResE * row_bytes + (FUSE ? 0u : (uint32_t)nt * row_bytes);
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         mbar_init_fence();
-        prefetch_l2(W + (size_t)e0 * n_embd, (uint64_t)kResE * row_bytes);
+        if (an.w_early) {
+            // The weight (the caller's, never written by the op just before
+            // it) is copied while the previous kernel runs; the barrier
+            // expects the token rows too, copied after the wait.
+            mbar_expect_tx(&bar, tx);
+            for (int j = 0; j < kResE; j++)
+                bulk_g2s(ws + (size_t)j * ldw, W + (size_t)(e0 + j) * n_embd, row_bytes, &bar);
+        } else {
+            prefetch_l2(W + (size_t)e0 * n_embd, (uint64_t)kResE * row_bytes);
+        }
         // The cluster's token rows: hints only (they may be the previous
         // kernel's output; they are read after the wait).
         prefetch_l2(x + t0 * n_embd, (uint64_t)nt * row_bytes);
@@ -444,8 +455,11 @@ __global__ void __launch_bounds__(res_threads(TOK), 1)
     pdl_wait();
     pdl_trigger();
     if (threadIdx.x == 0) {
-        mbar_expect_tx(&bar, kResE * row_bytes + (FUSE ? 0u : (uint32_t)nt * row_bytes));
-        for (int j = 0; j < kResE; j++) bulk_g2s(ws + (size_t)j * ldw, W + (size_t)(e0 + j) * n_embd, row_bytes, &bar);
+        if (!an.w_early) {
+            mbar_expect_tx(&bar, tx);
+            for (int j = 0; j < kResE; j++)
+                bulk_g2s(ws + (size_t)j * ldw, W + (size_t)(e0 + j) * n_embd, row_bytes, &bar);
+        }
         if constexpr (!FUSE)
             for (int k = 0; k < nt; k++) bulk_g2s(xs + (size_t)k * n_embd, x + (t0 + k) * n_embd, row_bytes, &bar);
     }
@@ -650,7 +664,7 @@ bool router_gemv_fast(int64_t n_tokens, int n_embd, int n_expert, int n_used, co
 
 cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const float *W, float *logits_out,
                                     int32_t *idx, float *scores, int64_t n_tokens, int n_embd, int n_expert,
-                                    int n_used, int norm_topk)
+                                    int n_used, int norm_topk, bool w_static)
 {
     if (n_tokens <= 0) return cudaSuccess;
     if (!idx && !logits_out) return cudaErrorInvalidValue;
@@ -659,7 +673,8 @@ cudaError_t launch_router_gemv_topk(const LaunchCtx &c, const float *x, const fl
         // by how many tokens it holds; up to kSmallT tokens (decode batches)
         // one token per compute warp keeps that chain 4x shorter.
         const cudaError_t er =
-            try_resident<false>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk, AddNorm{});
+            try_resident<false>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk,
+                                AddNorm{nullptr, nullptr, nullptr, nullptr, 0.0f, w_static ? 1 : 0});
         if (er != cudaErrorNotSupported) return er;
         if (n_tokens <= kSmallT)
             return launch_cluster<4, 4, 1, 4>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk);
@@ -689,7 +704,7 @@ cudaError_t launch_add_norm_router_topk(const LaunchCtx &c, const float *x, cons
 {
     if (n_tokens <= 0) return cudaSuccess;
     if (!add_norm_router_fast(n_tokens, n_embd, n_expert, n_used, x, r, W)) return cudaErrorInvalidValue;
-    const AddNorm an{r, norm_w, sum_out, norm_out, eps};
+    const AddNorm an{r, norm_w, sum_out, norm_out, eps, 1};
     const cudaError_t er = try_resident<true>(c, x, W, logits_out, idx, scores, n_tokens, n_embd, n_used, norm_topk, an);
     if (er != cudaErrorNotSupported) return er;
     if (n_tokens <= kSmallT)
